@@ -1,0 +1,333 @@
+// glq_api.cu -- the extern "C" boundary of libglq.so (declared in
+// include/glq.h): argument validation, path planning, per-device set-up,
+// dispatch to the kernels, path/status names and the device error word.
+//
+// Nothing here allocates device memory; the only device-resident state is the
+// per-device sticky error word below.  No C++ exception crosses the boundary.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstdint>
+#include <mutex>
+
+#include "glq_internal.h"
+
+namespace glq {
+namespace {
+
+// Sticky error word raised by kernels whose bounded waits expired.
+__device__ unsigned int g_device_error_word;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  std::once_flag once;
+  int status = GLQ_OK;  // glq_status of the set-up
+  int sm_count = 148;
+  unsigned int* error_word = nullptr;
+};
+
+DeviceState g_devices[kMaxDevices];
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_DEVICE;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return GLQ_ERR_DEVICE;
+  DeviceState& st = g_devices[dev];
+  std::call_once(st.once, [&st, dev] {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      st.status = GLQ_ERR_DEVICE;
+      return;
+    }
+    // The kernels are built for sm_100a only (compute capability 10.0).
+    if (major != 10 || minor != 0) {
+      st.status = GLQ_ERR_DEVICE;
+      return;
+    }
+    st.sm_count = sms > 0 ? sms : 148;
+    void* word = nullptr;
+    if (cudaGetSymbolAddress(&word, g_device_error_word) != cudaSuccess ||
+        tc_prepare_device() != cudaSuccess) {
+      cudaGetLastError();
+      st.status = GLQ_ERR_CUDA;
+      return;
+    }
+    st.error_word = static_cast<unsigned int*>(word);
+    st.status = GLQ_OK;
+  });
+  *out = &st;
+  return st.status;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int auto_split(int64_t tiles, int64_t k_blocks, int sm_count) {
+  int64_t s = sm_count / std::max<int64_t>(tiles, 1);
+  s = std::min<int64_t>(s, GLQ_MAX_SPLIT);
+  s = std::min<int64_t>(s, k_blocks);
+  // Each split keeps at least two K blocks so the pipeline has depth.
+  while (s > 1 && k_blocks / s < 2) --s;
+  return static_cast<int>(std::max<int64_t>(s, 1));
+}
+
+int validate(int dtype, int epilogue, int64_t m, int64_t n, int64_t k, int split_k) {
+  if (dtype != GLQ_DTYPE_F16 && dtype != GLQ_DTYPE_BF16) return GLQ_ERR_INVALID_ARGUMENT;
+  if (epilogue < GLQ_EPILOGUE_NONE || epilogue > GLQ_EPILOGUE_BIAS_SILU) return GLQ_ERR_INVALID_ARGUMENT;
+  if (m < 0 || n < 0 || k < 0) return GLQ_ERR_SHAPE;
+  if (m > INT_MAX || n > INT_MAX || k > INT_MAX) return GLQ_ERR_SHAPE;
+  if (split_k < 0 || split_k > GLQ_MAX_SPLIT) return GLQ_ERR_SPLIT;
+  return GLQ_OK;
+}
+
+}  // namespace
+
+int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
+  c->split = 1;
+  c->tile_t = 0;
+  if (p.m == 0 || p.n == 0) {
+    c->path = GLQ_PATH_EMPTY;
+    c->kernel = kKernelNone;
+    return GLQ_OK;
+  }
+  if (p.k == 0) {
+    c->path = GLQ_PATH_ZERO_K;
+    c->kernel = kKernelFill;
+    return GLQ_OK;
+  }
+  constexpr int64_t esz = 2;
+  const bool unit_inner = (p.a_cs == 1 || p.k == 1) && (p.b_ks == 1 || p.k == 1);
+  if (!unit_inner) {
+    c->path = GLQ_PATH_STRIDED;
+    c->kernel = kKernelGeneric;
+    return GLQ_OK;
+  }
+  // TMA / 128-bit loads: 16-byte aligned bases and row pitches, rows that do
+  // not overlap.
+  const bool w_ok = aligned16(p.b) && (p.n == 1 || (p.b_ns > 0 && (p.b_ns * esz) % 16 == 0 && p.b_ns >= p.k));
+  const bool a_ok = aligned16(p.a) && (p.m == 1 || (p.a_rs > 0 && (p.a_rs * esz) % 16 == 0 && p.a_rs >= p.k));
+  if (!w_ok || !a_ok) {
+    c->path = GLQ_PATH_UNALIGNED;
+    c->kernel = kKernelGeneric;
+    return GLQ_OK;
+  }
+  if (p.m == 1) {
+    c->kernel = kKernelGemv;
+    c->split = split_k > 0 ? split_k : 1;
+    c->path = (p.k % 8 != 0) ? GLQ_PATH_TAIL : GLQ_PATH_GEMV_M1;
+    return GLQ_OK;
+  }
+  c->kernel = kKernelTc;
+  c->tile_t = tc_token_tile(p.m);
+  const int64_t k_blocks = tc_k_blocks(p.k);
+  const int64_t tiles = ((p.n + 127) / 128) * ((p.m + c->tile_t - 1) / c->tile_t);
+  int s = split_k > 0 ? split_k : auto_split(tiles, k_blocks, sm_count > 0 ? sm_count : 148);
+  s = static_cast<int>(std::min<int64_t>(s, k_blocks));
+  c->split = std::max(s, 1);
+  if (p.n % 128 != 0 || p.k % 64 != 0) {
+    c->path = GLQ_PATH_TAIL;
+  } else {
+    c->path = c->split > 1 ? GLQ_PATH_TC_SPLITK : GLQ_PATH_TC;
+  }
+  return GLQ_OK;
+}
+
+}  // namespace glq
+
+using glq::Choice;
+using glq::Problem;
+
+extern "C" {
+
+int glq_plan(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride, const void* B,
+             int64_t b_k_stride, int64_t b_n_stride, int64_t y_row_stride, int64_t M, int64_t N,
+             int64_t K, int split_k, int sm_count, int* path_out, int* split_out) {
+  const int v = glq::validate(dtype, GLQ_EPILOGUE_NONE, M, N, K, split_k);
+  if (v != GLQ_OK) return v;
+  if (M > 1 && N > 0 && y_row_stride < N) return GLQ_ERR_OUTPUT_LAYOUT;
+  Problem p = {};
+  p.dtype = dtype;
+  p.a = A;
+  p.a_rs = a_row_stride;
+  p.a_cs = a_col_stride;
+  p.b = B;
+  p.b_ks = b_k_stride;
+  p.b_ns = b_n_stride;
+  p.ldy = y_row_stride;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  Choice c;
+  const int r = glq::plan_problem(p, split_k, sm_count, &c);
+  if (r != GLQ_OK) return r;
+  if (path_out) *path_out = c.path;
+  if (split_out) *split_out = c.split;
+  return GLQ_OK;
+}
+
+int glq_linear(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride, const void* B,
+               int64_t b_k_stride, int64_t b_n_stride, const void* bias, int epilogue, void* Y,
+               int64_t y_row_stride, int64_t M, int64_t N, int64_t K, int split_k, void* workspace,
+               size_t workspace_bytes, void* stream, int* path_out, int* split_out) {
+  int v = glq::validate(dtype, epilogue, M, N, K, split_k);
+  if (v != GLQ_OK) return v;
+  if (M > 0 && N > 0) {
+    if (Y == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
+    if (M > 1 && y_row_stride < N) return GLQ_ERR_OUTPUT_LAYOUT;
+    if (epilogue != GLQ_EPILOGUE_NONE && bias == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
+    if (K > 0 && (A == nullptr || B == nullptr)) return GLQ_ERR_INVALID_ARGUMENT;
+  }
+  Problem p = {};
+  p.dtype = dtype;
+  p.a = A;
+  p.a_rs = a_row_stride;
+  p.a_cs = a_col_stride;
+  p.b = B;
+  p.b_ks = b_k_stride;
+  p.b_ns = b_n_stride;
+  p.bias = bias;
+  p.epilogue = epilogue;
+  p.y = Y;
+  p.ldy = y_row_stride;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  p.partial = nullptr;
+
+  Choice c;
+  if (path_out) *path_out = GLQ_PATH_EMPTY;
+  if (split_out) *split_out = 1;
+  if (M == 0 || N == 0) {
+    return glq::plan_problem(p, split_k, 0, &c);
+  }
+  glq::DeviceState* dev = nullptr;
+  v = glq::device_state(&dev);
+  if (v != GLQ_OK) return v;
+  v = glq::plan_problem(p, split_k, dev->sm_count, &c);
+  if (v != GLQ_OK) return v;
+  if (workspace != nullptr && c.split > 1) {
+    const size_t need = static_cast<size_t>(c.split) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
+    if (workspace_bytes < need) return GLQ_ERR_WORKSPACE;
+    p.partial = static_cast<float*>(workspace);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  switch (c.kernel) {
+    case glq::kKernelFill: e = glq::launch_fill(p, s); break;
+    case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
+    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, dev->error_word, s); break;
+    case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
+    default: break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_CUDA;
+  }
+  if (path_out) *path_out = c.path;
+  if (split_out) *split_out = c.kernel == glq::kKernelGeneric ? 1 : c.split;
+  return GLQ_OK;
+}
+
+int glq_linear_f16(const void* A, int64_t lda, int64_t a_col_stride, const void* B,
+                   int64_t b_row_stride, int64_t b_col_stride, const void* bias, void* Y, int64_t ldy,
+                   int M, int N, int K, int split_k, void* workspace, size_t workspace_bytes,
+                   void* stream, int* path_out) {
+  return glq_linear(GLQ_DTYPE_F16, A, lda, a_col_stride, B, b_row_stride, b_col_stride, bias,
+                    bias != nullptr ? GLQ_EPILOGUE_BIAS_SILU : GLQ_EPILOGUE_NONE, Y, ldy, M, N, K,
+                    split_k, workspace, workspace_bytes, stream, path_out, nullptr);
+}
+
+int glq_matmul(int dtype, const void* a, const void* b, void* c, int m, int n, int k, void* stream) {
+  return glq_linear(dtype, a, k, 1, b, n, 1, nullptr, GLQ_EPILOGUE_NONE, c, n, m, n, k, 0, nullptr, 0,
+                    stream, nullptr, nullptr);
+}
+
+int glq_splitk_matmul(int dtype, const void* a, const void* b, void* c, int m, int n, int k,
+                      float* partial, int splits, void* stream) {
+  if (splits < 1 || splits > GLQ_MAX_SPLIT) return GLQ_ERR_SPLIT;
+  const size_t bytes = partial != nullptr ? glq_workspace_bytes(m, n, k, splits) : 0;
+  return glq_linear(dtype, a, k, 1, b, n, 1, nullptr, GLQ_EPILOGUE_NONE, c, n, m, n, k, splits, partial,
+                    bytes, stream, nullptr, nullptr);
+}
+
+size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k) {
+  if (M <= 0 || N <= 0 || K <= 0 || split_k < 0 || split_k > GLQ_MAX_SPLIT) return 0;
+  int s;
+  if (M == 1) {
+    s = split_k > 0 ? split_k : 1;
+  } else {
+    const int64_t kb = glq::tc_k_blocks(K);
+    const int bt = glq::tc_token_tile(M);
+    const int64_t tiles = ((N + 127) / 128) * ((M + bt - 1) / bt);
+    s = split_k > 0 ? split_k : glq::auto_split(tiles, kb, 148);
+    s = static_cast<int>(std::min<int64_t>(s, kb));
+  }
+  if (s <= 1) return 0;
+  return static_cast<size_t>(s) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
+}
+
+const char* glq_path_name(int path) {
+  switch (path) {
+    case GLQ_PATH_EMPTY: return "empty";
+    case GLQ_PATH_ZERO_K: return "zero_k";
+    case GLQ_PATH_GEMV_M1: return "gemv_m1";
+    case GLQ_PATH_TC: return "tc_tcgen05";
+    case GLQ_PATH_TC_SPLITK: return "tc_splitk";
+    case GLQ_PATH_TAIL: return "tail";
+    case GLQ_PATH_STRIDED: return "strided";
+    case GLQ_PATH_UNALIGNED: return "unaligned";
+    default: return "unknown";
+  }
+}
+
+const char* glq_status_string(int status) {
+  switch (status) {
+    case GLQ_OK: return "ok";
+    case GLQ_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer, dtype or epilogue)";
+    case GLQ_ERR_SHAPE: return "invalid shape or stride";
+    case GLQ_ERR_SPLIT: return "split_k must be in 0..8";
+    case GLQ_ERR_WORKSPACE: return "workspace smaller than split * M * N * 4 bytes";
+    case GLQ_ERR_OUTPUT_LAYOUT: return "output row stride smaller than N";
+    case GLQ_ERR_CUDA: return "CUDA runtime or driver call failed";
+    case GLQ_ERR_DEVICE: return "no usable device: the kernels need a compute capability 10.0 (sm_100a) GPU";
+    case GLQ_ERR_DEVICE_TIMEOUT: return "an in-kernel bounded wait expired";
+    default: return "unknown status";
+  }
+}
+
+int glq_device_error(unsigned int* word_out, int clear) {
+  if (word_out == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
+  glq::DeviceState* dev = nullptr;
+  const int v = glq::device_state(&dev);
+  if (v != GLQ_OK) return v;
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_CUDA;
+  }
+  unsigned int word = 0;
+  if (cudaMemcpy(&word, dev->error_word, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_CUDA;
+  }
+  if (clear && word != 0) {
+    if (cudaMemset(dev->error_word, 0, sizeof(word)) != cudaSuccess) {
+      cudaGetLastError();
+      return GLQ_ERR_CUDA;
+    }
+  }
+  *word_out = word;
+  return GLQ_OK;
+}
+
+int glq_abi_version(void) { return GLQ_ABI_VERSION; }
+
+const char* glq_build_target(void) { return "sm_100a"; }
+
+}  // extern "C"

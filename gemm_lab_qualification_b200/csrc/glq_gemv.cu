@@ -1,0 +1,175 @@
+// glq_gemv.cu -- M = 1 linear kernel: y[n] = epilogue(sum_k a[k] * W[n, k]).
+//
+// One token costs 2 flops per weight element, far below the tensor-core
+// ridge, so the weight stream is the whole cost.  Each warp reduces one W row
+// (or one of `split` contiguous K ranges of it): lanes issue 128-bit
+// streaming loads (ld.global.nc.L1::no_allocate) of consecutive 16-byte
+// chunks, UNROLL chunks per lane in flight before any arithmetic, accumulate
+// in FP32, and reduce with a fixed xor-shuffle tree.  With split > 1 the
+// partial sums of one row are merged by its first warp in split order
+// 0..split-1 through shared memory, so the result is deterministic; the
+// optional FP32 partials are written in the lab's [split, 1, N] layout.
+//
+// Reference counterpart: the M = 1 rows of the split-K and tiled kernels
+// (csrc/ptx_mma.cuh:502-770, kernels.py:324-393); the CTest case
+// 1x4096x4096 (CMakeLists.txt:45-51) exercises this shape.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "glq_internal.h"
+#include "glq_ptx.cuh"
+
+namespace glq {
+namespace {
+
+struct GemvArgs {
+  const void* a;
+  const void* w;
+  long long ldw;
+  const void* bias;
+  int epilogue;
+  void* y;
+  int n;
+  int k;
+  int split;
+  int rows_per_block;
+  float* partial;
+};
+
+__device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilogue) {
+  if (epilogue == GLQ_EPILOGUE_NONE) return acc;
+  const float v = acc + bias;
+  if (epilogue == GLQ_EPILOGUE_BIAS) return v;
+  return v / (1.0f + __expf(-v));
+}
+
+template <typename T>
+struct Vec;
+
+template <>
+struct Vec<__half> {
+  __device__ static float2 pair(uint32_t bits) {
+    __half2 h = *reinterpret_cast<const __half2*>(&bits);
+    return __half22float2(h);
+  }
+  __device__ static float to_f(__half v) { return __half2float(v); }
+  __device__ static __half from_f(float v) { return __float2half_rn(v); }
+};
+
+template <>
+struct Vec<__nv_bfloat16> {
+  __device__ static float2 pair(uint32_t bits) {
+    __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&bits);
+    return __bfloat1622float2(h);
+  }
+  __device__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <typename T>
+__device__ __forceinline__ void dot8(const uint4& w, const uint4& a, float& acc0, float& acc1) {
+  const float2 w0 = Vec<T>::pair(w.x), a0 = Vec<T>::pair(a.x);
+  const float2 w1 = Vec<T>::pair(w.y), a1 = Vec<T>::pair(a.y);
+  const float2 w2 = Vec<T>::pair(w.z), a2 = Vec<T>::pair(a.z);
+  const float2 w3 = Vec<T>::pair(w.w), a3 = Vec<T>::pair(a.w);
+  acc0 = fmaf(w0.x, a0.x, acc0);
+  acc1 = fmaf(w0.y, a0.y, acc1);
+  acc0 = fmaf(w1.x, a1.x, acc0);
+  acc1 = fmaf(w1.y, a1.y, acc1);
+  acc0 = fmaf(w2.x, a2.x, acc0);
+  acc1 = fmaf(w2.y, a2.y, acc1);
+  acc0 = fmaf(w3.x, a3.x, acc0);
+  acc1 = fmaf(w3.y, a3.y, acc1);
+}
+
+constexpr int kBlockThreadsMax = 256;
+
+template <typename T, int UNROLL>
+__global__ void __launch_bounds__(kBlockThreadsMax) gemv_kernel(const GemvArgs g) {
+  __shared__ float warp_sums[kBlockThreadsMax / 32];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = g.split;
+  const int row_slot = warp / split;
+  const int part = warp % split;
+  const long long n = static_cast<long long>(blockIdx.x) * g.rows_per_block + row_slot;
+
+  float acc0 = 0.0f, acc1 = 0.0f;
+  if (n < g.n) {
+    const T* wrow = static_cast<const T*>(g.w) + n * g.ldw;
+    const uint4* wv = reinterpret_cast<const uint4*>(wrow);
+    const uint4* av = reinterpret_cast<const uint4*>(g.a);
+    const int chunks = g.k >> 3;
+    const int c_begin = static_cast<int>((static_cast<long long>(part) * chunks) / split);
+    const int c_end = static_cast<int>((static_cast<long long>(part + 1) * chunks) / split);
+    for (int c = c_begin + lane; c < c_end; c += 32 * UNROLL) {
+      uint4 w[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int cc = c + u * 32;
+        w[u] = cc < c_end ? ptx::ldg_stream_v4(wv + cc) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int cc = c + u * 32;
+        if (cc < c_end) {
+          const uint4 a = __ldg(av + cc);
+          dot8<T>(w[u], a, acc0, acc1);
+        }
+      }
+    }
+    if (part == split - 1 && lane == 0) {
+      // K % 8 remainder, scalar, in ascending k.
+      const T* a = static_cast<const T*>(g.a);
+      for (int kk = chunks << 3; kk < g.k; ++kk) {
+        acc0 = fmaf(Vec<T>::to_f(wrow[kk]), Vec<T>::to_f(a[kk]), acc0);
+      }
+    }
+  }
+  float acc = acc0 + acc1;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) warp_sums[warp] = acc;
+  __syncthreads();
+  if (part == 0 && lane == 0 && n < g.n) {
+    float sum = 0.0f;
+    for (int p = 0; p < split; ++p) {
+      const float v = warp_sums[row_slot * split + p];
+      sum += v;
+      if (g.partial != nullptr) g.partial[static_cast<long long>(p) * g.n + n] = v;
+    }
+    float bias_v = 0.0f;
+    if (g.epilogue != GLQ_EPILOGUE_NONE) bias_v = Vec<T>::to_f(static_cast<const T*>(g.bias)[n]);
+    static_cast<T*>(g.y)[n] = Vec<T>::from_f(apply_epilogue(sum, bias_v, g.epilogue));
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gemv(const Problem& p, int split, unsigned int* /*err*/, cudaStream_t s) {
+  GemvArgs g;
+  g.a = p.a;
+  g.w = p.b;
+  g.ldw = p.b_ns;
+  g.bias = p.bias;
+  g.epilogue = p.epilogue;
+  g.y = p.y;
+  g.n = static_cast<int>(p.n);
+  g.k = static_cast<int>(p.k);
+  g.split = split;
+  const int warps_per_row = split;
+  int rows = (kBlockThreadsMax / 32) / warps_per_row;
+  if (rows < 1) rows = 1;
+  g.rows_per_block = rows;
+  g.partial = p.partial;
+  const unsigned threads = static_cast<unsigned>(rows * warps_per_row * 32);
+  const unsigned blocks = static_cast<unsigned>((p.n + rows - 1) / rows);
+  if (p.dtype == GLQ_DTYPE_BF16) {
+    gemv_kernel<__nv_bfloat16, 16><<<blocks, threads, 0, s>>>(g);
+  } else {
+    gemv_kernel<__half, 16><<<blocks, threads, 0, s>>>(g);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace glq

@@ -1,0 +1,185 @@
+// glq_generic.cu -- the explicit GPU paths for layouts the TMA/GEMV kernels
+// cannot address, and the K = 0 fill.
+//
+// generic_kernel: any element strides (transposed or padded views, the lab's
+// B = [K, N] row-major operand) and any alignment (odd base offsets, row
+// pitches that are not a multiple of 16 bytes such as K = 4090).  A 32 x 64
+// output tile per 256-thread CTA; A and B tiles are staged through shared
+// memory in FP32 with the unit-stride dimension mapped to consecutive
+// threads, and every thread accumulates its 2 x 4 outputs in ascending k.
+// Reference counterpart: the masked-load tile loop of _matmul_kernel
+// (kernels.py:103-129), which the lab only reaches for contiguous inputs
+// (kernels.py:143-144); strided views fell back to torch there
+// (qualification.py:58-64).
+//
+// fill_kernel: K = 0 makes every sum empty, so Y = epilogue(0 [+ bias]).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "glq_internal.h"
+
+namespace glq {
+namespace {
+
+template <typename T>
+struct Conv;
+template <>
+struct Conv<__half> {
+  __device__ static float to_f(__half v) { return __half2float(v); }
+  __device__ static __half from_f(float v) { return __float2half_rn(v); }
+};
+template <>
+struct Conv<__nv_bfloat16> {
+  __device__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilogue) {
+  if (epilogue == GLQ_EPILOGUE_NONE) return acc;
+  const float v = acc + bias;
+  if (epilogue == GLQ_EPILOGUE_BIAS) return v;
+  return v / (1.0f + __expf(-v));
+}
+
+struct GenericArgs {
+  const void* a;
+  long long a_rs, a_cs;
+  const void* b;
+  long long b_ks, b_ns;
+  const void* bias;
+  int epilogue;
+  void* y;
+  long long ldy;
+  long long m, n, k;
+  int a_k_fast;  // 1: consecutive threads walk k when loading A
+  int b_k_fast;  // 1: consecutive threads walk k when loading B
+};
+
+constexpr int kBM = 32, kBN = 64, kBK = 32, kThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) generic_kernel(const GenericArgs g) {
+  __shared__ float As[kBK][kBM + 1];
+  __shared__ float Bs[kBK][kBN + 1];
+  const int tid = threadIdx.x;
+  const long long m0 = static_cast<long long>(blockIdx.y) * kBM;
+  const long long n0 = static_cast<long long>(blockIdx.x) * kBN;
+  const int tm = tid >> 4;  // rows tm*2 .. tm*2+1
+  const int tn = tid & 15;  // cols tn + 16*j
+  const T* a = static_cast<const T*>(g.a);
+  const T* b = static_cast<const T*>(g.b);
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+
+  for (long long k0 = 0; k0 < g.k; k0 += kBK) {
+    for (int i = tid; i < kBM * kBK; i += kThreads) {
+      int r, c;
+      if (g.a_k_fast) {
+        r = i / kBK;
+        c = i % kBK;
+      } else {
+        c = i / kBM;
+        r = i % kBM;
+      }
+      const long long m = m0 + r, kk = k0 + c;
+      As[c][r] = (m < g.m && kk < g.k) ? Conv<T>::to_f(a[m * g.a_rs + kk * g.a_cs]) : 0.0f;
+    }
+    for (int i = tid; i < kBN * kBK; i += kThreads) {
+      int r, c;
+      if (g.b_k_fast) {
+        r = i / kBK;
+        c = i % kBK;
+      } else {
+        c = i / kBN;
+        r = i % kBN;
+      }
+      const long long nn = n0 + r, kk = k0 + c;
+      Bs[c][r] = (nn < g.n && kk < g.k) ? Conv<T>::to_f(b[kk * g.b_ks + nn * g.b_ns]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kBK; ++kk) {
+      const float a0 = As[kk][tm * 2], a1 = As[kk][tm * 2 + 1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float bv = Bs[kk][tn + 16 * j];
+        acc[0][j] = fmaf(a0, bv, acc[0][j]);
+        acc[1][j] = fmaf(a1, bv, acc[1][j]);
+      }
+    }
+    __syncthreads();
+  }
+
+  T* y = static_cast<T*>(g.y);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const long long m = m0 + tm * 2 + i;
+    if (m >= g.m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const long long nn = n0 + tn + 16 * j;
+      if (nn >= g.n) continue;
+      float bias_v = 0.0f;
+      if (g.epilogue != GLQ_EPILOGUE_NONE) bias_v = Conv<T>::to_f(static_cast<const T*>(g.bias)[nn]);
+      y[m * g.ldy + nn] = Conv<T>::from_f(apply_epilogue(acc[i][j], bias_v, g.epilogue));
+    }
+  }
+}
+
+template <typename T>
+__global__ void fill_kernel(T* y, long long ldy, long long m, long long n, const T* bias, int epilogue) {
+  const long long total = m * n;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / n, c = i % n;
+    const float bias_v = epilogue != GLQ_EPILOGUE_NONE ? Conv<T>::to_f(bias[c]) : 0.0f;
+    y[r * ldy + c] = Conv<T>::from_f(apply_epilogue(0.0f, bias_v, epilogue));
+  }
+}
+
+long long abs_ll(long long v) { return v < 0 ? -v : v; }
+
+}  // namespace
+
+cudaError_t launch_generic(const Problem& p, cudaStream_t s) {
+  GenericArgs g;
+  g.a = p.a;
+  g.a_rs = p.a_rs;
+  g.a_cs = p.a_cs;
+  g.b = p.b;
+  g.b_ks = p.b_ks;
+  g.b_ns = p.b_ns;
+  g.bias = p.bias;
+  g.epilogue = p.epilogue;
+  g.y = p.y;
+  g.ldy = p.ldy;
+  g.m = p.m;
+  g.n = p.n;
+  g.k = p.k;
+  g.a_k_fast = abs_ll(p.a_cs) <= abs_ll(p.a_rs) || p.m == 1;
+  g.b_k_fast = abs_ll(p.b_ks) <= abs_ll(p.b_ns) || p.n == 1;
+  const dim3 grid(static_cast<unsigned>((p.n + kBN - 1) / kBN), static_cast<unsigned>((p.m + kBM - 1) / kBM));
+  if (p.dtype == GLQ_DTYPE_BF16) {
+    generic_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(g);
+  } else {
+    generic_kernel<__half><<<grid, kThreads, 0, s>>>(g);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill(const Problem& p, cudaStream_t s) {
+  const long long total = p.m * p.n;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  if (p.dtype == GLQ_DTYPE_BF16) {
+    fill_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<__nv_bfloat16*>(p.y), p.ldy, p.m, p.n, static_cast<const __nv_bfloat16*>(p.bias),
+        p.epilogue);
+  } else {
+    fill_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<__half*>(p.y), p.ldy, p.m, p.n, static_cast<const __half*>(p.bias), p.epilogue);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace glq

@@ -1,0 +1,85 @@
+// glq_internal.h -- declarations shared by the kernel translation units and
+// the C-ABI layer of libglq.so.  Not installed; include/glq.h is the public
+// surface.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/glq.h"
+
+namespace glq {
+
+// Bits of the per-device sticky error word (glq_device_error).
+enum DeviceErrorBits : unsigned int {
+  kErrTimeoutProducer = 1u << 0,  // TMA producer gave up waiting for a free stage
+  kErrTimeoutMma = 1u << 1,       // MMA issuer gave up waiting for a filled stage
+  kErrTimeoutEpilogue = 1u << 2,  // epilogue gave up waiting for the accumulator
+  kErrTimeoutDrain = 1u << 3,     // in-flight TMA loads did not land at exit
+  kErrSmemAlign = 1u << 4,        // dynamic shared memory not 1024-B aligned
+};
+
+// Time budget of one bounded in-kernel wait.  Legitimate waits last
+// microseconds; this only ends a wait that can no longer complete.
+constexpr uint64_t kWaitBudgetNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+// One linear problem after argument validation.  Strides in elements.
+struct Problem {
+  int dtype;  // glq_dtype
+  const void* a;
+  int64_t a_rs, a_cs;
+  const void* b;
+  int64_t b_ks, b_ns;
+  const void* bias;
+  int epilogue;  // glq_epilogue
+  void* y;
+  int64_t ldy;
+  int64_t m, n, k;
+  float* partial;  // optional [split, m, n] FP32 split partials
+};
+
+// Path selection result.
+struct Choice {
+  int path;     // glq_path
+  int split;    // K ranges merged in-kernel (1 = none)
+  int kernel;   // Kernel below
+  int tile_t;   // token tile (MMA N) of the tcgen05 kernel
+};
+
+enum Kernel : int {
+  kKernelNone = 0,
+  kKernelFill = 1,
+  kKernelGemv = 2,
+  kKernelTc = 3,
+  kKernelGeneric = 4,
+};
+
+// Pure host planning (glq_plan and glq_linear share it).
+int plan_problem(const Problem& p, int split_k, int sm_count, Choice* out);
+
+// Number of 64-wide K blocks of the tcgen05 kernel.
+inline int64_t tc_k_blocks(int64_t k) { return (k + 63) / 64; }
+
+// Token tile of the tcgen05 kernel for m tokens.
+inline int tc_token_tile(int64_t m) {
+  if (m <= 16) return 16;
+  if (m <= 32) return 32;
+  if (m <= 64) return 64;
+  if (m <= 128) return 128;
+  return 256;
+}
+
+// Launchers (return cudaError_t of the launch).  err = device error word.
+cudaError_t launch_fill(const Problem& p, cudaStream_t s);
+cudaError_t launch_gemv(const Problem& p, int split, unsigned int* err, cudaStream_t s);
+cudaError_t launch_generic(const Problem& p, cudaStream_t s);
+// Returns cudaErrorNotSupported-style codes through `status` for TMA encode
+// problems (GLQ_ERR_CUDA).
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, unsigned int* err, cudaStream_t s);
+
+// Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).
+cudaError_t tc_prepare_device();
+
+}  // namespace glq

@@ -1,0 +1,196 @@
+/*
+ * glq.h -- C ABI of the B200 (sm_100a) linear fragment library, libglq.so.
+ *
+ * The library computes the FP16/BF16 linear fragment of the GEMM lab:
+ *
+ *     Y[m, n] = epilogue( sum_k A[m, k] * B[k, n] )        (FP32 accumulate)
+ *
+ * where B is the lab's [K, N] operand.  A weight matrix stored the way a
+ * linear layer stores it, W[N, K] row-major (K-contiguous), is the B operand
+ * viewed as W^T, i.e. b_k_stride = 1 and b_n_stride = ldw.  That K-contiguous
+ * view is the primary fast layout; the lab's own B[K, N] row-major layout
+ * (b_k_stride = N, b_n_stride = 1) is accepted through the same entry point.
+ *
+ * Every entry point is stateless apart from a per-device one-time set-up
+ * (kernel attributes, the TMA encoder entry point), thread-safe, stream-ordered
+ * on the caller's stream, never allocates device memory and never throws
+ * across the boundary: each returns a glq_status.  All pointers are device
+ * pointers unless stated otherwise.  `stream` is a cudaStream_t (NULL is the
+ * legacy default stream).
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   - gemm_lab::launch_* (csrc/ptx_mma.cuh:220,772,796,827,931,978,1031):
+ *     void launch_X(const T* a, const T* b, T* c, int m, int n, int k,
+ *                   cudaStream_t) with B = [K, N] row-major.
+ *   - gemm_lab::launch_ptx_mma_splitk (csrc/ptx_mma.cuh:931-965) and
+ *     ptx_mma_splitk_workspace_bytes (csrc/ptx_mma.cuh:926-929).
+ *   - The Triton operator bodies of kernels.py (triton_matmul_into
+ *     kernels.py:148-171, triton_bias_silu_into kernels.py:252-280,
+ *     triton_splitk_matmul_into kernels.py:396-441) that the Python binding
+ *     of this library re-exports under the same names.
+ *   - Error convention: GEMM_LAB_CUDA_CHECK (include/gemm_lab/cuda_check.hpp:
+ *     39-65) throws std::runtime_error; here the same failures are returned
+ *     as status codes and glq_status_string() gives the text.
+ */
+#ifndef GLQ_H_
+#define GLQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLQ_ABI_VERSION 1
+
+/* Element types (inputs, bias and output share one type). */
+enum glq_dtype {
+  GLQ_DTYPE_F16 = 0,
+  GLQ_DTYPE_BF16 = 1
+};
+
+/* Epilogue applied in FP32 before the single store of Y.
+ * GLQ_EPILOGUE_BIAS_SILU is y = v * sigmoid(v), v = acc + bias[n]
+ * (kernels.py:191-249, _matmul_bias_silu_kernel). */
+enum glq_epilogue {
+  GLQ_EPILOGUE_NONE = 0,
+  GLQ_EPILOGUE_BIAS = 1,
+  GLQ_EPILOGUE_BIAS_SILU = 2
+};
+
+/* GPU path taken by one call; reported through path_out.  Every path is a
+ * GPU kernel of this library (or no launch at all for "empty"). */
+enum glq_path {
+  GLQ_PATH_EMPTY = 0,     /* M == 0 or N == 0: nothing to write, no launch */
+  GLQ_PATH_ZERO_K = 1,    /* K == 0: fill kernel writes epilogue(0 [+ bias]) */
+  GLQ_PATH_GEMV_M1 = 2,   /* M == 1, K-contiguous W: vectorised warp GEMV */
+  GLQ_PATH_TC = 3,        /* tcgen05 + TMA + TMEM GEMM, no K split */
+  GLQ_PATH_TC_SPLITK = 4, /* same, K split across a cluster, DSMEM merge */
+  GLQ_PATH_TAIL = 5,      /* tcgen05 or GEMV kernel on a ragged N/K edge */
+  GLQ_PATH_STRIDED = 6,   /* generic kernel: non-unit inner stride */
+  GLQ_PATH_UNALIGNED = 7, /* generic kernel: rows or base not 16-B aligned */
+  GLQ_PATH_COUNT = 8
+};
+
+enum glq_status {
+  GLQ_OK = 0,
+  GLQ_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad dtype/epilogue value */
+  GLQ_ERR_SHAPE = 2,            /* negative or too large M/N/K, bad strides */
+  GLQ_ERR_SPLIT = 3,            /* split_k outside 0..GLQ_MAX_SPLIT */
+  GLQ_ERR_WORKSPACE = 4,        /* workspace given but smaller than needed */
+  GLQ_ERR_OUTPUT_LAYOUT = 5,    /* y_row_stride < N */
+  GLQ_ERR_CUDA = 6,             /* CUDA runtime or driver call failed */
+  GLQ_ERR_DEVICE = 7,           /* no device, or not a compute 10.0 GPU */
+  GLQ_ERR_DEVICE_TIMEOUT = 8,   /* an in-kernel bounded wait expired */
+  GLQ_STATUS_COUNT = 9
+};
+
+#define GLQ_MAX_SPLIT 8
+
+/*
+ * glq_linear -- the one general entry point.
+ *
+ *   A[m, k]   at A + m * a_row_stride + k * a_col_stride        (elements)
+ *   B[k, n]   at B + k * b_k_stride   + n * b_n_stride          (elements)
+ *   bias[n]   at bias + n (contiguous; required unless epilogue NONE)
+ *   Y[m, n]   at Y + m * y_row_stride + n                        (unit column stride)
+ *
+ * split_k: 0 = library choice; 1..GLQ_MAX_SPLIT = split the K reduction into
+ *   that many contiguous ranges merged in-kernel in split order (the merge is
+ *   deterministic).  A path that cannot split reports split 1.
+ * workspace: optional (may be NULL).  When non-NULL it receives the FP32
+ *   per-split partial sums in the lab's [split, M, N] layout
+ *   (kernels.py:431-439), and must hold glq_workspace_bytes() bytes.  The
+ *   merge itself never needs it.
+ * path_out, split_out: optional host pointers receiving the path taken and
+ *   the split count used.
+ *
+ * Replaces: gemm_lab::launch_* / launch_ptx_mma_splitk (csrc/ptx_mma.cuh:
+ *   220-965) and the launch bodies of kernels.py:148-171, 252-280, 396-441.
+ */
+int glq_linear(int dtype,
+               const void* A, int64_t a_row_stride, int64_t a_col_stride,
+               const void* B, int64_t b_k_stride, int64_t b_n_stride,
+               const void* bias, int epilogue,
+               void* Y, int64_t y_row_stride,
+               int64_t M, int64_t N, int64_t K,
+               int split_k, void* workspace, size_t workspace_bytes,
+               void* stream, int* path_out, int* split_out);
+
+/*
+ * glq_linear_f16 -- FP16 form with the argument order of the lab's proposed
+ * native shim: A with (lda, a_col_stride), B with (b_row_stride = k stride,
+ * b_col_stride = n stride), nullable bias selecting bias+SiLU.
+ * Replaces: triton_bias_silu_into / triton_matmul_into (kernels.py:148-171,
+ * 252-280) for FP16.
+ */
+int glq_linear_f16(const void* A, int64_t lda, int64_t a_col_stride,
+                   const void* B, int64_t b_row_stride, int64_t b_col_stride,
+                   const void* bias, void* Y, int64_t ldy,
+                   int M, int N, int K, int split_k,
+                   void* workspace, size_t workspace_bytes,
+                   void* stream, int* path_out);
+
+/*
+ * glq_matmul -- C = A * B for contiguous row-major A[M, K], B[K, N],
+ * C[M, N] of `dtype`.  Replaces the launch signature shared by every native
+ * implementation: void launch_X(const T* a, const T* b, T* c, int m, int n,
+ * int k, cudaStream_t) (csrc/ptx_mma.cuh:220,772,796,827,978,1031).
+ */
+int glq_matmul(int dtype, const void* a, const void* b, void* c,
+               int m, int n, int k, void* stream);
+
+/*
+ * glq_splitk_matmul -- forced split-K C = A * B (contiguous row-major), the
+ * per-split FP32 partials written to `partial` ([splits, M, N]) and merged
+ * in-kernel.  Replaces launch_ptx_mma_splitk(a, b, c, m, n, k, partial,
+ * splits, stream) (csrc/ptx_mma.cuh:931-965).  partial may be NULL.
+ */
+int glq_splitk_matmul(int dtype, const void* a, const void* b, void* c,
+                      int m, int n, int k, float* partial, int splits,
+                      void* stream);
+
+/*
+ * glq_workspace_bytes -- bytes of the optional partial-sum workspace for a
+ * call of this shape with this split_k (0 = the library's choice for a
+ * K-contiguous problem).  Replaces ptx_mma_splitk_workspace_bytes
+ * (csrc/ptx_mma.cuh:926-929) and TritonSplitKPlan.workspace_bytes
+ * (kernels.py:461-464).  Pure host function.
+ */
+size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k);
+
+/*
+ * glq_plan -- the path and split a glq_linear call with these arguments
+ * would take, without launching anything (pure host function; pointer
+ * arguments are only inspected for alignment).  Replaces the per-call path
+ * selection of qualification.path (qualification.py:58-59) and
+ * ptx_mma_split_count (csrc/ptx_mma.cuh:889-924).  sm_count 0 = 148.
+ */
+int glq_plan(int dtype,
+             const void* A, int64_t a_row_stride, int64_t a_col_stride,
+             const void* B, int64_t b_k_stride, int64_t b_n_stride,
+             int64_t y_row_stride, int64_t M, int64_t N, int64_t K,
+             int split_k, int sm_count, int* path_out, int* split_out);
+
+/* Names of paths and statuses (static strings, never NULL). */
+const char* glq_path_name(int path);
+const char* glq_status_string(int status);
+
+/*
+ * glq_device_error -- read (and with clear != 0, reset) the sticky error word
+ * that this library's kernels set when a bounded in-kernel wait expires, for
+ * the current device.  Synchronises the device.  *word_out is 0 when no
+ * kernel has reported a problem.
+ */
+int glq_device_error(unsigned int* word_out, int clear);
+
+/* ABI version (GLQ_ABI_VERSION) and the compiled target, e.g. "sm_100a". */
+int glq_abi_version(void);
+const char* glq_build_target(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* GLQ_H_ */

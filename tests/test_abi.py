@@ -1,0 +1,203 @@
+"""The C ABI of libglq.so without a GPU: symbols, names, planning, validation.
+
+Every symbol include/glq.h declares must be exported; path planning
+(glq_plan) and workspace sizing are pure host functions and are checked here
+against the rules the kernels rely on.  No compute call runs on the CPU:
+a real launch request returns GLQ_ERR_DEVICE when there is no sm_100a GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+from gemm_lab_qualification_b200 import _native as native
+
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "glq.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(glq_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = native.library()
+    names = declared_functions()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(native.SIGNATURES), "binding and header disagree"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(native.LIBRARY_PATH)], capture_output=True, text=True)
+    if out.returncode == 0:
+        exported = set(re.findall(r"\b(glq_[a-z0-9_]+)\b", out.stdout))
+        assert set(names) <= exported
+
+
+def test_abi_version_and_target():
+    lib = native.library()
+    assert lib.glq_abi_version() == 1
+    assert lib.glq_build_target() == b"sm_100a"
+
+
+def test_path_and_status_names():
+    assert [native.path_name(i) for i in range(len(native.PATHS))] == list(native.PATHS)
+    assert native.path_name(99) == "unknown"
+    for status in range(len(native.STATUS_NAMES)):
+        assert native.status_string(status)
+    assert native.status_string(0) == "ok"
+
+
+def plan(m, n, k, a_strides=None, b_strides=None, a_ptr=0, b_ptr=0, split=0, ldy=None, dtype=0, sms=148):
+    a_strides = a_strides or (k, 1)
+    b_strides = b_strides or (1, k)  # W[N, K].T: the K-contiguous fast layout
+    return native.plan(dtype, a_ptr, a_strides, b_ptr, b_strides, ldy if ldy is not None else n, m, n, k,
+                       split, sms)
+
+
+@pytest.mark.parametrize("m,expected", [(1, ("gemv_m1", 1)), (8, ("tc_splitk", 4)), (32, ("tc_splitk", 4)),
+                                        (128, ("tc_splitk", 4))])
+def test_plan_decode_sweep(m, expected):
+    assert plan(m, 4096, 4096) == expected
+
+
+def test_plan_boundaries():
+    assert plan(0, 4096, 4096)[0] == "empty"
+    assert plan(32, 0, 4096)[0] == "empty"
+    assert plan(32, 4096, 0)[0] == "zero_k"
+    assert plan(32, 4093, 4096)[0] == "tail"
+    # K = 4090 contiguous: row pitch 8180 B is not a multiple of 16 -> no TMA.
+    assert plan(32, 4096, 4090)[0] == "unaligned"
+    # K = 4090 in rows padded to 4096 elements: TMA with OOB zero fill.
+    assert plan(32, 4096, 4090, a_strides=(4096, 1), b_strides=(1, 4096))[0] == "tail"
+    # padded rows (K + 8) keep 16-byte pitches.
+    assert plan(32, 4096, 4096, a_strides=(4104, 1))[0] == "tc_splitk"
+    assert plan(32, 4096, 4096, b_strides=(1, 4104))[0] == "tc_splitk"
+    # transposed A, the reference's own B = [K, N] layout -> generic kernel.
+    assert plan(32, 4096, 4096, a_strides=(1, 32))[0] == "strided"
+    assert plan(32, 4096, 4096, b_strides=(4096, 1))[0] == "strided"
+    assert plan(1, 4096, 4096, b_strides=(4096, 1))[0] == "strided"
+    # base one element off 16-byte alignment.
+    assert plan(32, 4096, 4096, a_ptr=2)[0] == "unaligned"
+    assert plan(1, 4096, 4096, b_ptr=2)[0] == "unaligned"
+
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("split", [2, 4, 8])
+def test_plan_forced_split(m, split):
+    path, s = plan(m, 4096, 4096, split=split)
+    assert s == split
+    assert path == ("gemv_m1" if m == 1 else "tc_splitk")
+
+
+def test_plan_split_clamped_to_k_blocks():
+    # K = 100 has two 64-wide blocks: a forced split of 8 becomes 2.
+    assert plan(32, 4096, 100, a_strides=(104, 1), b_strides=(1, 104), split=8) == ("tail", 2)
+    # one block: no split possible.
+    assert plan(32, 4096, 64, split=8) == ("tc_tcgen05", 1)
+
+
+def test_plan_auto_split_tracks_sm_count():
+    assert plan(32, 4096, 4096, sms=148) == ("tc_splitk", 4)
+    assert plan(32, 4096, 4096, sms=64) == ("tc_splitk", 2)
+    assert plan(32, 4096, 4096, sms=32) == ("tc_tcgen05", 1)
+    # prefill: 16 x 8 = 128 tiles already fill the device.
+    assert plan(4096, 1024, 8192) == ("tc_tcgen05", 1)
+    # sharded MLP slice 28672 / 8 = 3584 rows: 28 tiles -> split 5.
+    assert plan(32, 3584, 8192) == ("tc_splitk", 5)
+
+
+def test_plan_rejects_bad_arguments():
+    with pytest.raises(native.GlqError) as e:
+        plan(32, 4096, 4096, split=9)
+    assert e.value.status == 3
+    with pytest.raises(native.GlqError) as e:
+        plan(-1, 4096, 4096)
+    assert e.value.status == 2
+    with pytest.raises(native.GlqError) as e:
+        plan(32, 4096, 4096, dtype=7)
+    assert e.value.status == 1
+    with pytest.raises(native.GlqError) as e:
+        plan(32, 4096, 4096, ldy=100)
+    assert e.value.status == 5
+
+
+def test_workspace_bytes():
+    assert native.workspace_bytes(32, 4096, 4096, 0) == 4 * 32 * 4096 * 4
+    assert native.workspace_bytes(8, 4096, 4096, 8) == 8 * 8 * 4096 * 4
+    assert native.workspace_bytes(1, 4096, 4096, 0) == 0
+    assert native.workspace_bytes(1, 4096, 4096, 4) == 4 * 4096 * 4
+    assert native.workspace_bytes(32, 4096, 4096, 1) == 0
+    assert native.workspace_bytes(0, 4096, 4096, 4) == 0
+    assert native.workspace_bytes(32, 4096, 4096, 9) == 0
+
+
+def test_linear_validation_precedes_device_use():
+    lib = native.library()
+    path = ctypes.c_int(-1)
+    split = ctypes.c_int(-1)
+    # bad dtype / epilogue / split / shapes / null pointers: no device needed.
+    assert lib.glq_linear(5, None, 0, 1, None, 1, 0, None, 0, None, 0, 1, 1, 1, 0, None, 0, None, None, None) == 1
+    assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 9, None, 0, 1, 1, 1, 0, None, 0, None, None, None) == 1
+    assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 1, 1, 1, 9, None, 0, None, None, None) == 3
+    assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, -1, 1, 1, 0, None, 0, None, None, None) == 2
+    assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 1, 1, 1, 0, None, 0, None, None, None) == 1
+    # bias+SiLU without a bias pointer
+    assert lib.glq_linear(0, 16, 1, 1, 16, 1, 1, None, 2, 16, 1, 1, 1, 1, 0, None, 0, None, None, None) == 1
+    # empty problems succeed without touching a device and report "empty"
+    assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 0, 8, 8, 0, None, 0, None,
+                          ctypes.byref(path), ctypes.byref(split)) == 0
+    assert native.PATHS[path.value] == "empty" and split.value == 1
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device status on a GPU-less host")
+def test_compute_call_without_gpu_fails_loudly():
+    lib = native.library()
+    status = lib.glq_linear(0, 16, 8, 1, 16, 1, 8, None, 0, 32, 8, 2, 8, 8, 0, None, 0, None, None, None)
+    assert status == 7  # GLQ_ERR_DEVICE: no CPU fallback exists
+    a = torch.zeros(2, 8, dtype=torch.float16)
+    with pytest.raises(native.GlqError):
+        native.linear(a, a.t(), torch.empty(2, 2, dtype=torch.float16))
+
+
+def test_operator_api_contract_errors_on_cpu():
+    """ValueError contract of kernels.py:132-145 / 396-409."""
+    from gemm_lab_qualification_b200 import kernels
+    a = torch.zeros(4, 8, dtype=torch.float16)
+    b = torch.zeros(8, 3, dtype=torch.float16)
+    with pytest.raises(ValueError, match="requires CUDA tensors"):
+        kernels.triton_matmul(a, b)
+    with pytest.raises(ValueError, match="rank-2"):
+        kernels.triton_matmul(a[0], b)
+    with pytest.raises(ValueError, match="incompatible dimensions"):
+        kernels.triton_matmul(a, b[:4])
+    with pytest.raises(ValueError, match="split_k must be 2, 4, or 8"):
+        kernels.triton_splitk_matmul_into(a, b, None, None, split_k=3)
+    with pytest.raises(ValueError, match="split_k must be 2, 4, or 8"):
+        kernels.TritonSplitKPlan(a, b, 16)
+
+
+def test_custom_ops_registered_with_fake_kernels():
+    from gemm_lab_qualification_b200 import kernels  # noqa: F401  (registers the ops)
+    for name in ["triton_matmul", "triton_splitk_matmul", "triton_adaptive_matmul", "adaptive_matmul",
+                 "triton_bias_silu", "adaptive_bias_silu"]:
+        assert hasattr(torch.ops.gemm_lab, name), name
+    with torch._subclasses.fake_tensor.FakeTensorMode():
+        a = torch.empty(4, 8, dtype=torch.float16, device="cuda")
+        b = torch.empty(8, 3, dtype=torch.float16, device="cuda")
+        bias = torch.empty(3, dtype=torch.float16, device="cuda")
+        assert torch.ops.gemm_lab.triton_matmul(a, b).shape == (4, 3)
+        assert torch.ops.gemm_lab.triton_bias_silu(a, b, bias).shape == (4, 3)
+
+
+def test_adaptive_path_names_native_kernel():
+    from gemm_lab_qualification_b200 import kernels
+    assert kernels.adaptive_path(8, 4096, 4096, torch.float16) == "tc_splitk"
+    assert kernels.adaptive_path(1, 4096, 4096) == "gemv_m1"
+    assert kernels.adaptive_bias_silu_path(8, 11008, 4096, torch.float16) == "tc_tcgen05"

@@ -1,0 +1,297 @@
+"""GPU parity: the sm_100a kernels against the CPU FP64 oracle.
+
+Every call goes through the C ABI (include/glq.h) via the operator API.  The
+gates are the reference's: the seed-7 uniform corpus at
+abs <= 0.02 + 0.002 * |ref|; the reference corpus (seed 1729) at
+0.003 + 0.005 * |ref| and the fused epilogue at 0.01 + 0.01 * |ref|
+(qualification.py:47-56, 95-98).  Output canaries (123-filled guards,
+qualification.py:90-94) and NaN-poisoned input storage are checked bit-exact.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import f16
+from gemm_lab_qualification_b200 import _native as native
+from gemm_lab_qualification_b200 import kernels, workloads
+from oracle import reference as oracle
+
+pytestmark = pytest.mark.gpu
+
+U_ATOL, U_RTOL = oracle.UNIFORM_ATOL, oracle.UNIFORM_RTOL
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def guarded_output(m: int, n: int, dtype, device, pitch: int | None = None):
+    """Output view inside a 123-filled guard buffer (qualification.py:90-94)."""
+    pitch = n if pitch is None else pitch
+    rows = max(m, 1)
+    guard = torch.full((rows * pitch + 32,), 123, dtype=dtype, device=device)
+    out = guard[16:16 + rows * pitch].view(rows, pitch)[:m, :n]
+    return guard, out
+
+
+def assert_guard_intact(guard: torch.Tensor, m: int, n: int, pitch: int | None = None):
+    pitch = n if pitch is None else pitch
+    g = guard.cpu()
+    assert (g[:16] == 123).all() and (g[-16:] == 123).all(), "output canary overwritten"
+    if pitch > n and m > 0:
+        body = g[16:16 + m * pitch].view(m, pitch)
+        assert (body[:, n:] == 123).all(), "row padding of the output overwritten"
+
+
+@pytest.fixture(autouse=True)
+def clean_error_word(cuda_device):
+    native.device_error(clear=True)
+    yield
+    assert native.device_error(clear=True) == 0, "a bounded in-kernel wait expired"
+
+
+# ------------------------------------------------------------------ BASELINE sweep
+
+@pytest.mark.parametrize("m", [1, 8, 32, 128])
+def test_uniform_sweep_fused(cuda_device, golden, m):
+    arrays, _ = golden
+    a, w, bias = workloads.uniform_inputs(m, 4096, 4096)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    guard, out = guarded_output(m, 4096, torch.float16, cuda_device)
+    kernels.triton_bias_silu_into(da, dw.t(), db, out)
+    path = kernels.last_path()
+    assert path == (("gemv_m1", 1) if m == 1 else ("tc_splitk", 4))
+    torch.cuda.synchronize()
+    expected = oracle.linear_reference(a, w, bias, silu=True)
+    oracle.compare(host(out), expected, U_ATOL, U_RTOL)
+    rows = arrays[f"uniform/m{m}/rows"]
+    oracle.compare(host(out)[rows], arrays[f"uniform/m{m}/fused_rows"], U_ATOL, U_RTOL)
+    assert_guard_intact(guard, m, 4096)
+
+
+@pytest.mark.parametrize("m", [1, 8, 32, 128])
+def test_uniform_sweep_plain(cuda_device, golden, m):
+    arrays, _ = golden
+    a, w, _ = workloads.uniform_inputs(m, 4096, 4096)
+    da, dw = a.to(cuda_device), w.to(cuda_device)
+    out = torch.empty((m, 4096), dtype=torch.float16, device=cuda_device)
+    kernels.triton_matmul_into(da, dw.t(), out)
+    expected = oracle.linear_reference(a, w)
+    oracle.compare(host(out), expected, U_ATOL, U_RTOL)
+    rows = arrays[f"uniform/m{m}/rows"]
+    oracle.compare(host(out)[rows], arrays[f"uniform/m{m}/expected_rows"], U_ATOL, U_RTOL)
+
+
+def test_uniform_small_golden(cuda_device, golden):
+    arrays, _ = golden
+    a = torch.from_numpy(f16(arrays["uniform/small/a"]).copy()).to(cuda_device)
+    w = torch.from_numpy(f16(arrays["uniform/small/w"]).copy()).to(cuda_device)
+    bias = torch.from_numpy(f16(arrays["uniform/small/bias"]).copy()).to(cuda_device)
+    out = kernels.triton_bias_silu(a, w.t(), bias)
+    assert kernels.last_path()[0] in ("tc_tcgen05", "tc_splitk")
+    oracle.compare(host(out), arrays["uniform/small/fused"], U_ATOL, U_RTOL)
+    out = kernels.triton_matmul(a, w.t())
+    oracle.compare(host(out), arrays["uniform/small/expected"], U_ATOL, U_RTOL)
+
+
+def test_determinism_bitwise(cuda_device):
+    a, w, bias = workloads.uniform_inputs(32, 4096, 4096)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    outs = [kernels.triton_bias_silu(da, dw.t(), db) for _ in range(3)]
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
+
+
+# ------------------------------------------------------------------ reference corpus
+
+def corpus_cases():
+    for shape in workloads.MANIFEST["edges"]:
+        for pattern in workloads.MANIFEST["edge_patterns"]:
+            for layout in workloads.MANIFEST["layouts"]:
+                yield shape, pattern, layout
+
+
+@pytest.mark.parametrize("shape,pattern,layout", list(corpus_cases()),
+                         ids=[f"{s['id']}-{p}-{l}" for s, p, l in corpus_cases()])
+def test_reference_corpus(cuda_device, golden, shape, pattern, layout):
+    """qualification.check() records (qualification.py:74-99), native kernels."""
+    arrays, _ = golden
+    key = f"edge/{shape['id']}/{pattern}"
+    expected = arrays[key + "/expected"]
+    a, b = workloads.inputs(shape, pattern, layout)
+    if layout == "strided":
+        da = workloads.poisoned_view(a, "strided", cuda_device)
+        db = workloads.poisoned_view(b, "strided", cuda_device)
+    else:
+        da, db = a.to(cuda_device), b.to(cuda_device)
+    bases = [t._base if t._base is not None else t for t in (da, db)]
+    snapshots = [t.clone() for t in bases]
+    m, n = shape["m"], shape["n"]
+    guard, out = guarded_output(m, n, torch.float16, cuda_device)
+    kernels.triton_matmul_into(da, db, out)
+    oracle.compare(host(out), expected)
+    assert_guard_intact(guard, m, n)
+    path = kernels.last_path()[0]
+    if m == 0 or n == 0:
+        assert path == "empty"
+    elif shape["k"] == 0:
+        assert path == "zero_k"
+    if m and n:
+        bias = workloads.reference_bias(n, device=cuda_device)
+        fused = kernels.triton_bias_silu(da, db, bias)
+        oracle.compare(host(fused), arrays[key + "/fused"], oracle.FUSED_ATOL, oracle.FUSED_RTOL)
+    # inputs and their NaN-poisoned padding are untouched, bit for bit
+    for base, snap in zip(bases, snapshots):
+        assert torch.equal(base.view(torch.int16), snap.view(torch.int16))
+
+
+def padded_pitch_view(x: torch.Tensor, device) -> torch.Tensor:
+    """Rows padded to a 16-byte pitch (+8 elements), NaN in the gap."""
+    rows, cols = x.shape
+    pitch = ((cols + 7) // 8) * 8 + 8
+    store = torch.full((rows, pitch), float("nan"), dtype=x.dtype, device=device)
+    store[:, :cols] = x.to(device)
+    return store[:, :cols]
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 257, 131), (129, 257, 65), (17, 31, 13), (300, 200, 520),
+                                   (2, 128, 64), (512, 512, 512)])
+def test_tcgen05_tails_in_padded_rows(cuda_device, m, n, k):
+    """Ragged M/N/K on the TMA path (OOB zero fill, masked epilogue)."""
+    g = torch.Generator().manual_seed(m * 1000 + n + k)
+    a = (torch.rand((m, k), generator=g) - .5).half()
+    w = (torch.rand((n, k), generator=g) - .5).half()
+    bias = (torch.rand((n,), generator=g) - .5).half()
+    da = padded_pitch_view(a, cuda_device)
+    dw = padded_pitch_view(w, cuda_device)
+    db = bias.to(cuda_device)
+    pitch = ((n + 7) // 8) * 8 + 8
+    guard, out = guarded_output(m, n, torch.float16, cuda_device, pitch=pitch)
+    kernels.triton_bias_silu_into(da, dw.t(), db, out)
+    path = kernels.last_path()[0]
+    assert path in ("tc_tcgen05", "tc_splitk", "tail", "gemv_m1")
+    oracle.compare(host(out), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+    assert_guard_intact(guard, m, n, pitch=pitch)
+
+
+# ------------------------------------------------------------------ boundary probes
+
+def probe_inputs(probe, device):
+    m, n, k = probe["m"], probe["n"], probe["k"]
+    a, w, bias = workloads.uniform_inputs(m, n, k)
+    layout = probe["layout"]
+    da, dw = a.to(device), w.to(device)
+    if layout == "a_padded":
+        da = workloads.poisoned_view(a, "padded", device)
+    elif layout == "w_padded":
+        dw = workloads.poisoned_view(w, "padded", device)
+    elif layout == "a_transposed":
+        da = workloads.poisoned_view(a, "transposed", device)
+    elif layout == "a_offset":
+        da = workloads.poisoned_view(a, "offset", device)
+    return a, w, bias, da, dw, bias.to(device)
+
+
+EXPECTED_PROBE_PATH = {"zero-m": "empty", "zero-k": "zero_k", "tail-n": "tail", "tail-k": "unaligned",
+                       "a-row-stride": "tc_splitk", "w-row-stride": "tc_splitk",
+                       "a-transposed": "strided", "misaligned-base": "unaligned"}
+
+
+@pytest.mark.parametrize("probe", workloads.MANIFEST["probes"], ids=[p["id"] for p in workloads.MANIFEST["probes"]])
+def test_boundary_probe(cuda_device, probe):
+    a, w, bias, da, dw, db = probe_inputs(probe, cuda_device)
+    m, n = probe["m"], probe["n"]
+    guard, out = guarded_output(m, n, torch.float16, cuda_device)
+    before_a = da.clone()
+    kernels.triton_bias_silu_into(da, dw.t(), db, out)
+    assert kernels.last_path()[0] == EXPECTED_PROBE_PATH[probe["id"]]
+    assert_guard_intact(guard, m, n)
+    assert torch.equal(da.view(torch.int16), before_a.view(torch.int16)), "input modified"
+    if m:
+        expected = oracle.linear_reference(a, w, bias, silu=True, samples=8)
+        oracle.compare(host(out), expected, U_ATOL, U_RTOL)
+
+
+# ------------------------------------------------------------------ split-K probes
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("split", [2, 4, 8])
+def test_split_probe(cuda_device, m, split):
+    a, w, _ = workloads.uniform_inputs(m, 4096, 4096)
+    da, dw = a.to(cuda_device), w.to(cuda_device)
+    partial = torch.full((split, m, 4096), float("nan"), dtype=torch.float32, device=cuda_device)
+    out = torch.empty((m, 4096), dtype=torch.float16, device=cuda_device)
+    kernels.triton_splitk_matmul_into(da, dw.t(), partial, out, split)
+    assert kernels.last_path() == (("gemv_m1" if m == 1 else "tc_splitk"), split)
+    oracle.compare(host(out), oracle.linear_reference(a, w), U_ATOL, U_RTOL)
+    granule = 8 if m == 1 else 64
+    parts = oracle.split_partials_reference(a, w.t(), split, granule)
+    got = partial.cpu().double().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - parts).max() <= 1e-3 + 1e-4 * np.abs(parts).max()
+    # the FP32 merge of the partials in split order reproduces the output bits
+    merged = partial[0].clone()
+    for s in range(1, split):
+        merged = merged + partial[s]
+    assert torch.equal(merged.half().view(torch.int16), out.view(torch.int16))
+
+
+def test_splitk_plan_and_default(cuda_device):
+    a, w, _ = workloads.uniform_inputs(8, 4096, 4096)
+    da, dw = a.to(cuda_device), w.to(cuda_device)
+    plan = kernels.TritonSplitKPlan(da, dw.t(), 8)
+    assert plan.workspace_bytes() == 8 * 8 * 4096 * 4
+    out = plan()
+    oracle.compare(host(out), oracle.linear_reference(a, w), U_ATOL, U_RTOL)
+    out2 = kernels.triton_splitk_matmul(da, dw.t())
+    assert kernels.last_path() == ("tc_splitk", 4)
+    oracle.compare(host(out2), oracle.linear_reference(a, w), U_ATOL, U_RTOL)
+
+
+# ------------------------------------------------------------------ layouts, dtypes, ops
+
+def test_reference_layout_b_kn(cuda_device):
+    """The lab's own B = [K, N] row-major operand is an explicit GPU path."""
+    a, w, bias = workloads.uniform_inputs(8, 4096, 4096)
+    da, db_kn, dbias = a.to(cuda_device), w.t().contiguous().to(cuda_device), bias.to(cuda_device)
+    out = kernels.triton_bias_silu(da, db_kn, dbias)
+    assert kernels.last_path()[0] == "strided"
+    oracle.compare(host(out), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+
+
+@pytest.mark.parametrize("m", [1, 32])
+def test_bf16(cuda_device, m):
+    a, w, bias = workloads.uniform_inputs(m, 4096, 4096, dtype=torch.bfloat16)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    out = kernels.triton_bias_silu(da, dw.t(), db)
+    expected = oracle.linear_reference(a, w, bias, silu=True)
+    oracle.compare(host(out), expected, 0.05, 0.01)
+
+
+def test_custom_ops_and_plans(cuda_device):
+    a, w, bias = workloads.uniform_inputs(32, 4096, 4096)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    ref_plain = oracle.linear_reference(a, w)
+    ref_fused = oracle.linear_reference(a, w, bias, silu=True)
+    oracle.compare(host(torch.ops.gemm_lab.triton_matmul(da, dw.t())), ref_plain, U_ATOL, U_RTOL)
+    oracle.compare(host(torch.ops.gemm_lab.triton_splitk_matmul(da, dw.t())), ref_plain, U_ATOL, U_RTOL)
+    oracle.compare(host(torch.ops.gemm_lab.adaptive_matmul(da, dw.t())), ref_plain, U_ATOL, U_RTOL)
+    oracle.compare(host(torch.ops.gemm_lab.triton_bias_silu(da, dw.t(), db)), ref_fused, U_ATOL, U_RTOL)
+    oracle.compare(host(torch.ops.gemm_lab.adaptive_bias_silu(da, dw.t(), db)), ref_fused, U_ATOL, U_RTOL)
+    oracle.compare(host(kernels.TritonMatmulPlan(da, dw.t())()), ref_plain, U_ATOL, U_RTOL)
+    oracle.compare(host(kernels.TritonBiasSiluPlan(da, dw.t(), db)()), ref_fused, U_ATOL, U_RTOL)
+    oracle.compare(host(kernels.AdaptiveMatmulPlan(da, dw.t())()), ref_plain, U_ATOL, U_RTOL)
+
+
+def test_bias_only_epilogue_and_streams(cuda_device):
+    a, w, bias = workloads.uniform_inputs(16, 1024, 2048)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        out = torch.empty((16, 1024), dtype=torch.float16, device=cuda_device)
+        kernels.linear_into(da, dw.t(), out, db)
+    stream.synchronize()
+    expected = oracle.linear_reference(a, w) + bias.double().numpy()[None, :]
+    oracle.compare(host(out), expected, U_ATOL, U_RTOL)
