@@ -9,9 +9,12 @@ on its own rotating copy of W so that every call streams W from HBM (the
 copies together exceed the L2).  The headline ``value`` is the p50 device
 latency of the fused M = 32 call; ``sweep`` holds every M.
 
-Timing: each step starts behind a short GPU hold so all eight launches are
-queued before the device reaches them; every call is bracketed by its own CUDA
-events on the launching stream (device time, no host dispatch gaps).
+Timing (the reference's evidence.torch_measure protocol, inner = 10): a
+sample is one event pair on the launching stream around 10 back-to-back calls
+of one variant, each call on the next rotating W copy, queued behind a short
+GPU hold so host dispatch never shows in the span; per-call time = span / 10.
+The isolated single-call latency (inner = 1, includes the device-side launch
+latency of one kernel) is reported next to it in ``sweep``.
 
 Also reported: the roofline of the dominant kernel against the measured HBM
 peak (MEASURED_PEAKS.json), warm-L2 numbers (one W copy), an end-to-end number
@@ -67,6 +70,7 @@ def parse_args(argv=None):
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--inner", type=int, default=10, help="back-to-back calls per timed sample")
     p.add_argument("--sweep", type=str, default=",".join(map(str, SWEEP_M)),
                    help="comma-separated M values of the step (default 1,8,32,128)")
     return p.parse_args(argv)
@@ -266,15 +270,27 @@ def single_gpu(args, torch, dev) -> dict:
         return run
 
     fns = {f"{v}/m{m}": call(m, v) for m in sweep_m for v in ("fused", "plain")}
-    device_measure(fns, rounds=args.warmup)
+    device_measure(fns, rounds=args.warmup, inner=args.inner)
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clocks:
         t0 = time.perf_counter()
-        raw = device_measure(fns, rounds=args.steps)
+        raw = device_measure(fns, rounds=args.steps, inner=args.inner)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
-    warm = device_measure({k: call(int(k.split("/m")[1]), k.split("/")[0], rotate=False) for k in fns},
-                          rounds=max(10, args.steps // 4))
+    isolated = device_measure(fns, rounds=max(10, args.steps // 4), inner=1)
+    # Launch modes of the fused calls: without programmatic dependent launch,
+    # and with the inference declaration that W is static.
+    modes = {}
+    fused_fns = {k: f for k, f in fns.items() if k.startswith("fused/")}
+    for label, opts in (("no_pdl", {"pdl": False}), ("static_weights", {"static_weights": True})):
+        with kernels.launch_options(**opts):
+            modes[label] = device_measure(fused_fns, rounds=max(10, args.steps // 3), inner=args.inner)
+    # Warm L2: one variant at a time on a single W copy (32 MiB fits in L2).
+    warm = {}
+    for key in fns:
+        m_key, v_key = int(key.split("/m")[1]), key.split("/")[0]
+        warm.update(device_measure({key: call(m_key, v_key, rotate=False)}, rounds=max(5, args.steps // 10),
+                                   inner=args.inner))
 
     peak, peak_src = measured_hbm_peak()
     sweep = {}
@@ -293,6 +309,9 @@ def single_gpu(args, torch, dev) -> dict:
             row[f"{v}_gbs"] = gbs
             row[f"{v}_frac"] = gbs / peak
             row[f"{v}_warm_l2_p50_us"] = statistics.median(warm[f"{v}/m{m}"]) * 1e3
+            row[f"{v}_isolated_p50_us"] = statistics.median(isolated[f"{v}/m{m}"]) * 1e3
+        for label, samples in modes.items():
+            row[f"fused_{label}_p50_us"] = statistics.median(samples[f"fused/m{m}"]) * 1e3
         sweep[str(m)] = row
 
     head = sweep[str(args.m)]
@@ -304,10 +323,10 @@ def single_gpu(args, torch, dev) -> dict:
                 "traffic": traffic, "peak_source": peak_src,
                 "kernel": f"{kernel_tag} (fused, M={args.m}, path {head['path']}, split {head['split']})",
                 "algorithmic_bytes_per_launch": head["bytes_fused"], "launch_mean_us": head["fused_mean_us"]}
-    ms_per_step = sum(statistics.fmean(v) for v in raw.values())
+    ms_per_step = sum(statistics.fmean(v) for v in raw.values()) * args.inner
     return {"value": head["fused_p50_us"], "ms_per_step": ms_per_step, "sweep": sweep, "roofline": roofline,
             "clocks": clocks.summary(), "copies": copies, "l2_bytes": l2, "wall_s": wall,
-            "gpu_launches": args.steps * len(fns), "state": state}
+            "gpu_launches": args.steps * len(fns) * args.inner, "state": state}
 
 
 def e2e_public_api(args, torch, dev, rounds: int) -> dict:
@@ -388,17 +407,17 @@ def multi_gpu(args, torch, dist, dev, world: int, rank: int) -> dict:
     if not bool((err <= 0.02 + 0.002 * ref.abs()).all()):
         raise SystemExit(f"rank {rank}: sharded correctness gate failed")
     path = kernels.last_path()
-    device_measure({"step": step}, rounds=args.warmup)
+    device_measure({"step": step}, rounds=args.warmup, inner=args.inner)
     dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clocks:
-        raw = device_measure({"step": step}, rounds=args.steps)["step"]
+        raw = device_measure({"step": step}, rounds=args.steps, inner=args.inner)["step"]
         torch.cuda.synchronize()
     dist.barrier()
     p50 = torch.tensor([statistics.median(raw), statistics.fmean(raw)], dtype=torch.float64, device=dev)
     dist.all_reduce(p50, op=dist.ReduceOp.MAX)
     return {"value": float(p50[0]) * 1e3, "ms_per_step": float(p50[1]), "path": path, "clocks": clocks.summary(),
-            "shard_rows": ns, "copies": copies, "gpu_launches": args.steps}
+            "shard_rows": ns, "copies": copies, "gpu_launches": args.steps * args.inner}
 
 
 def run_native(args) -> int:
@@ -448,7 +467,10 @@ def run_native(args) -> int:
             "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": DATA,
             "config": {"workload": f"fused linear+bias+SiLU y=SiLU(A W^T + b), value at M={args.m}; step = "
-                                   f"M in {list(SWEEP_M)} x {{fused, plain}}, N=K=4096, W [N,K] K-contiguous",
+                                   f"M in {list(SWEEP_M)} x {{fused, plain}}, {args.inner} back-to-back calls each, "
+                                   f"N=K=4096, W [N,K] K-contiguous",
+                       "timing": f"CUDA events around {args.inner} back-to-back calls behind a GPU hold, p50 of "
+                                 f"span/{args.inner}",
                        "m": args.m, "n": N_DIM, "k": K_DIM, "parallelism": "single GPU",
                        "l2": f"inputs larger than L2: {res['copies']} rotating W copies "
                              f"({res['copies'] * 32} MiB) > L2 {res['l2_bytes'] / 2**20:.0f} MiB"},

@@ -24,6 +24,8 @@ STATUS_OK = 0
 STATUS_NAMES = ("ok", "invalid_argument", "shape", "split", "workspace", "output_layout", "cuda",
                 "device", "device_timeout")
 MAX_SPLIT = 8
+FLAG_NO_PDL = 1 << 0
+FLAG_STATIC_WEIGHTS = 1 << 1
 
 # Every symbol include/glq.h declares, with (restype, argtypes).
 _I64 = ctypes.c_int64
@@ -33,6 +35,8 @@ _PINT = ctypes.POINTER(ctypes.c_int)
 SIGNATURES = {
     "glq_linear": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _VP, _INT, _VP, _I64, _I64, _I64,
                           _I64, _INT, _VP, ctypes.c_size_t, _VP, _PINT, _PINT]),
+    "glq_linear_ex": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _VP, _INT, _VP, _I64, _I64, _I64,
+                             _I64, _INT, _VP, ctypes.c_size_t, _VP, ctypes.c_uint, _PINT, _PINT]),
     "glq_linear_f16": (_INT, [_VP, _I64, _I64, _VP, _I64, _I64, _VP, _VP, _I64, _INT, _INT, _INT,
                               _INT, _VP, ctypes.c_size_t, _VP, _PINT]),
     "glq_matmul": (_INT, [_INT, _VP, _VP, _VP, _INT, _INT, _INT, _VP]),
@@ -119,7 +123,7 @@ def plan(dtype: int, a_ptr: int, a_strides: tuple[int, int], b_ptr: int, b_strid
 
 def linear(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, bias: torch.Tensor | None = None,
            epilogue: int = EPILOGUE_NONE, split_k: int = 0, workspace: torch.Tensor | None = None,
-           stream: torch.cuda.Stream | None = None) -> tuple[str, int]:
+           stream: torch.cuda.Stream | None = None, flags: int = 0) -> tuple[str, int]:
     """out = epilogue(a @ b [+ bias]) through glq_linear on the current stream.
 
     a: [M, K], b: [K, N] (any strides; W[N, K].T is the K-contiguous fast
@@ -134,16 +138,16 @@ def linear(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, bias: torch.Tens
     ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     path = ctypes.c_int(-1)
     split = ctypes.c_int(0)
-    status = library().glq_linear(
+    status = library().glq_linear_ex(
         dtype_code(a.dtype),
         a.data_ptr(), a.stride(0), a.stride(1),
         b.data_ptr(), b.stride(0), b.stride(1),
         bias.data_ptr() if bias is not None else None, epilogue,
         out.data_ptr(), out.stride(0),
-        m, n, k, split_k, ws_ptr, ws_bytes, handle,
+        m, n, k, split_k, ws_ptr, ws_bytes, handle, flags,
         ctypes.byref(path), ctypes.byref(split))
     if status != STATUS_OK:
-        raise GlqError(status, "glq_linear")
+        raise GlqError(status, "glq_linear_ex")
     return PATHS[path.value], split.value
 
 

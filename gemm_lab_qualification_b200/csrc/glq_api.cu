@@ -176,8 +176,18 @@ int glq_linear(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_str
                int64_t b_k_stride, int64_t b_n_stride, const void* bias, int epilogue, void* Y,
                int64_t y_row_stride, int64_t M, int64_t N, int64_t K, int split_k, void* workspace,
                size_t workspace_bytes, void* stream, int* path_out, int* split_out) {
+  return glq_linear_ex(dtype, A, a_row_stride, a_col_stride, B, b_k_stride, b_n_stride, bias, epilogue, Y,
+                       y_row_stride, M, N, K, split_k, workspace, workspace_bytes, stream, 0u, path_out,
+                       split_out);
+}
+
+int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride, const void* B,
+                  int64_t b_k_stride, int64_t b_n_stride, const void* bias, int epilogue, void* Y,
+                  int64_t y_row_stride, int64_t M, int64_t N, int64_t K, int split_k, void* workspace,
+                  size_t workspace_bytes, void* stream, unsigned int flags, int* path_out, int* split_out) {
   int v = glq::validate(dtype, epilogue, M, N, K, split_k);
   if (v != GLQ_OK) return v;
+  if ((flags & ~(GLQ_FLAG_NO_PDL | GLQ_FLAG_STATIC_WEIGHTS)) != 0) return GLQ_ERR_INVALID_ARGUMENT;
   if (M > 0 && N > 0) {
     if (Y == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
     if (M > 1 && y_row_stride < N) return GLQ_ERR_OUTPUT_LAYOUT;
@@ -200,6 +210,7 @@ int glq_linear(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_str
   p.n = N;
   p.k = K;
   p.partial = nullptr;
+  p.flags = flags;
 
   Choice c;
   if (path_out) *path_out = GLQ_PATH_EMPTY;

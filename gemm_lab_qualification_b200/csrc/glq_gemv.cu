@@ -4,11 +4,15 @@
 // ridge, so the weight stream is the whole cost.  Each warp reduces one W row
 // (or one of `split` contiguous K ranges of it): lanes issue 128-bit
 // streaming loads (ld.global.nc.L1::no_allocate) of consecutive 16-byte
-// chunks, UNROLL chunks per lane in flight before any arithmetic, accumulate
+// chunks, UNROLL chunks per lane in flight before any arithmetic (registers
+// capped so four 256-thread blocks fit per SM: N = 4096 rows is one wave on
+// 148 SMs), accumulate
 // in FP32, and reduce with a fixed xor-shuffle tree.  With split > 1 the
 // partial sums of one row are merged by its first warp in split order
 // 0..split-1 through shared memory, so the result is deterministic; the
 // optional FP32 partials are written in the lab's [split, 1, N] layout.
+//
+// Launched with programmatic dependent launch (see glq.h, glq_flags).
 //
 // Reference counterpart: the M = 1 rows of the split-K and tiled kernels
 // (csrc/ptx_mma.cuh:502-770, kernels.py:324-393); the CTest case
@@ -34,13 +38,14 @@ struct GemvArgs {
   int split;
   int rows_per_block;
   float* partial;
+  unsigned int flags;
 };
 
 __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilogue) {
   if (epilogue == GLQ_EPILOGUE_NONE) return acc;
   const float v = acc + bias;
   if (epilogue == GLQ_EPILOGUE_BIAS) return v;
-  return v / (1.0f + __expf(-v));
+  return __fdividef(v, 1.0f + __expf(-v));
 }
 
 template <typename T>
@@ -85,7 +90,7 @@ __device__ __forceinline__ void dot8(const uint4& w, const uint4& a, float& acc0
 constexpr int kBlockThreadsMax = 256;
 
 template <typename T, int UNROLL>
-__global__ void __launch_bounds__(kBlockThreadsMax) gemv_kernel(const GemvArgs g) {
+__global__ void __launch_bounds__(kBlockThreadsMax, 4) gemv_kernel(const GemvArgs g) {
   __shared__ float warp_sums[kBlockThreadsMax / 32];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -95,20 +100,31 @@ __global__ void __launch_bounds__(kBlockThreadsMax) gemv_kernel(const GemvArgs g
   const long long n = static_cast<long long>(blockIdx.x) * g.rows_per_block + row_slot;
 
   float acc0 = 0.0f, acc1 = 0.0f;
-  if (n < g.n) {
-    const T* wrow = static_cast<const T*>(g.w) + n * g.ldw;
-    const uint4* wv = reinterpret_cast<const uint4*>(wrow);
-    const uint4* av = reinterpret_cast<const uint4*>(g.a);
-    const int chunks = g.k >> 3;
-    const int c_begin = static_cast<int>((static_cast<long long>(part) * chunks) / split);
-    const int c_end = static_cast<int>((static_cast<long long>(part + 1) * chunks) / split);
-    for (int c = c_begin + lane; c < c_end; c += 32 * UNROLL) {
-      uint4 w[UNROLL];
+  const bool row_ok = n < g.n;
+  const T* wrow = static_cast<const T*>(g.w) + (row_ok ? n : 0) * g.ldw;
+  const uint4* wv = reinterpret_cast<const uint4*>(wrow);
+  const uint4* av = reinterpret_cast<const uint4*>(g.a);
+  const int chunks = g.k >> 3;
+  const int c_begin = static_cast<int>((static_cast<long long>(part) * chunks) / split);
+  const int c_end = row_ok ? static_cast<int>((static_cast<long long>(part + 1) * chunks) / split) : c_begin;
+  uint4 w[UNROLL];
+  auto load_w = [&](int c0) {
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        const int cc = c + u * 32;
-        w[u] = cc < c_end ? ptx::ldg_stream_v4(wv + cc) : make_uint4(0u, 0u, 0u, 0u);
-      }
+    for (int u = 0; u < UNROLL; ++u) {
+      const int cc = c0 + u * 32;
+      w[u] = cc < c_end ? ptx::ldg_stream_v4(wv + cc) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // Programmatic dependent launch: a, bias and y wait for the predecessor
+  // grid; the first weight chunks may be requested before that when the
+  // caller declared the weights static.
+  const bool static_w = (g.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
+  if (static_w) load_w(c_begin + lane);
+  ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
+  if (row_ok) {
+    if (!static_w) load_w(c_begin + lane);
+    for (int c = c_begin + lane; c < c_end; c += 32 * UNROLL) {
 #pragma unroll
       for (int u = 0; u < UNROLL; ++u) {
         const int cc = c + u * 32;
@@ -117,6 +133,7 @@ __global__ void __launch_bounds__(kBlockThreadsMax) gemv_kernel(const GemvArgs g
           dot8<T>(w[u], a, acc0, acc1);
         }
       }
+      if (c + 32 * UNROLL < c_end) load_w(c + 32 * UNROLL);
     }
     if (part == split - 1 && lane == 0) {
       // K % 8 remainder, scalar, in ascending k.
@@ -162,14 +179,19 @@ cudaError_t launch_gemv(const Problem& p, int split, unsigned int* /*err*/, cuda
   if (rows < 1) rows = 1;
   g.rows_per_block = rows;
   g.partial = p.partial;
-  const unsigned threads = static_cast<unsigned>(rows * warps_per_row * 32);
-  const unsigned blocks = static_cast<unsigned>((p.n + rows - 1) / rows);
-  if (p.dtype == GLQ_DTYPE_BF16) {
-    gemv_kernel<__nv_bfloat16, 16><<<blocks, threads, 0, s>>>(g);
-  } else {
-    gemv_kernel<__half, 16><<<blocks, threads, 0, s>>>(g);
-  }
-  return cudaGetLastError();
+  g.flags = p.flags;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((p.n + rows - 1) / rows), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(rows * warps_per_row * 32), 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 0 : 1;
+  if (p.dtype == GLQ_DTYPE_BF16) return cudaLaunchKernelEx(&cfg, gemv_kernel<__nv_bfloat16, 8>, g);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<__half, 8>, g);
 }
 
 }  // namespace glq

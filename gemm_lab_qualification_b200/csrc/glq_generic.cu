@@ -38,7 +38,7 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilo
   if (epilogue == GLQ_EPILOGUE_NONE) return acc;
   const float v = acc + bias;
   if (epilogue == GLQ_EPILOGUE_BIAS) return v;
-  return v / (1.0f + __expf(-v));
+  return __fdividef(v, 1.0f + __expf(-v));
 }
 
 struct GenericArgs {

@@ -38,6 +38,7 @@ struct Problem {
   int64_t ldy;
   int64_t m, n, k;
   float* partial;  // optional [split, m, n] FP32 split partials
+  unsigned int flags;  // glq_flags
 };
 
 // Path selection result.

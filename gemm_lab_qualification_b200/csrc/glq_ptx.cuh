@@ -156,6 +156,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+// Warp-collective TMEM load: 8 consecutive 32-bit columns per lane.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -203,6 +212,17 @@ __device__ __forceinline__ void cluster_sync() {
           : "memory");
 }
 
+// Split-phase cluster barrier: arrive without ordering (used once all
+// threads have started, so a later wait proves every CTA is resident) ...
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+// ... and the matching wait.
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_byte_addr, uint32_t rank) {
   uint32_t r;
@@ -210,10 +230,24 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_byte_addr, uint32_
   return r;
 }
 
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-  return v;
+// 16-byte store into the shared memory of another CTA of the cluster.  The
+// store does not wait for completion; a later cluster barrier with release /
+// acquire semantics makes it visible to the owner.
+__device__ __forceinline__ void st_dsmem_v4(uint32_t cluster_addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (no-op without the launch
+// attribute), and allow the next grid to begin launching.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- loads

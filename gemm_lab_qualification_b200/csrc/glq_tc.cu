@@ -7,17 +7,25 @@
 // Design (swap-AB, decode shapes are weight-bandwidth bound):
 //   * W rows fill the 128-lane MMA M dimension; the token batch is the MMA N
 //     dimension (16..256), so M = 1..128 tokens cost one W pass.
-//   * One CTA = 128 threads owns a 128-row W tile x a token tile x one
-//     contiguous range of 64-wide K blocks.  Warp 0 lane 0 issues TMA loads
-//     (128-byte swizzle, K-major) into a STAGES-deep mbarrier ring; warp 1
-//     allocates TMEM and lane 0 issues tcgen05.mma; all four warps run the
-//     epilogue from TMEM (lane = W row, column = token).
+//   * One CTA = 256 threads owns a 128-row W tile x a token tile x one
+//     contiguous range of 64-wide K blocks.  Thread 0 starts the TMA stream
+//     (128-byte swizzle, K-major) into a STAGES-deep mbarrier ring before
+//     anything else; warp 1 allocates TMEM and lane 0 issues tcgen05.mma; all
+//     eight warps run the epilogue from TMEM (lane = W row, column = token),
+//     two warps per 32-lane TMEM quarter splitting the token columns.
 //   * Split-K: the K ranges of one tile are the CTAs of one thread-block
-//     cluster.  After the main loop each CTA stages its FP32 partial tile in
-//     its own shared memory; after a cluster barrier CTA r reduces token
-//     columns [r*T/S, (r+1)*T/S) by reading the S partials over DSMEM in
-//     split order 0..S-1, applies bias + SiLU and stores.  The merge order is
-//     fixed, so results are bitwise reproducible, and nothing waits on a flag.
+//     cluster.  After the main loop every CTA pushes each 4-token group of
+//     its FP32 partial tile to the CTA that owns the group (16-byte DSMEM
+//     stores, no round trip); after one cluster barrier each owner sums the S
+//     partials of its groups in split order 0..S-1 from its own shared
+//     memory, applies bias + SiLU and stores.  The merge order is fixed, so
+//     results are bitwise reproducible, and nothing waits on a flag.
+//   * Programmatic dependent launch: every thread waits for the predecessor
+//     grid (griddepcontrol.wait) before touching global memory and then lets
+//     the next grid launch, so back-to-back calls overlap launch latency,
+//     barrier set-up and TMEM allocation with the predecessor's tail.  With
+//     GLQ_FLAG_STATIC_WEIGHTS the first W stages are requested before the
+//     wait.
 //   * Every mbarrier wait is bounded (glq_ptx.cuh); on expiry the CTA raises
 //     a bit in the device error word, stops issuing work, drains its own
 //     in-flight TMA loads (bounded), still takes part in both cluster
@@ -65,13 +73,14 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilo
   if (epilogue == GLQ_EPILOGUE_NONE) return acc;
   const float v = acc + bias;
   if (epilogue == GLQ_EPILOGUE_BIAS) return v;
-  return v / (1.0f + __expf(-v));  // SiLU = v * sigmoid(v)
+  return __fdividef(v, 1.0f + __expf(-v));  // SiLU = v * sigmoid(v)
 }
 
 constexpr int kTileN = 128;  // W rows per CTA (MMA M, TMEM lanes)
 constexpr int kTileK = 64;   // K elements per stage: one 128-byte swizzle row
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr uint32_t kWTileBytes = kTileN * kTileK * 2;
+constexpr uint32_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
 
 template <int BT>
 struct TcConfig {
@@ -81,12 +90,9 @@ struct TcConfig {
   static constexpr int kStages = BT <= 64 ? 8 : (BT <= 128 ? 6 : 4);
   static constexpr uint32_t kTmemCols = BT < 32 ? 32 : BT;
   static constexpr uint32_t kPipeBytes = kStages * kStageBytes;
-  static constexpr uint32_t kXchgBytes = BT * kTileN * 4;
-  static constexpr uint32_t kBodyBytes = kPipeBytes > kXchgBytes ? kPipeBytes : kXchgBytes;
   static constexpr uint32_t kBarrierBytes = (2 * kStages + 1) * 8 + 16;
-  static constexpr uint32_t kSmemBytes = 1024 + kBodyBytes + kBarrierBytes;
   static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-B aligned");
-  static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static_assert(1024 + kPipeBytes + kBarrierBytes <= kSmemLimit, "pipeline exceeds shared memory");
 };
 
 struct TcArgs {
@@ -99,7 +105,18 @@ struct TcArgs {
   long long ldy;
   float* partial;
   unsigned int* err;
+  uint32_t recv_offset;     // split-K receive buffer, bytes from the 1024-aligned base
+  uint32_t recv_pitch4;     // its row pitch in 16-byte units (odd: conflict-free v4 stores)
+  int recv_overlaps;        // 1: it reuses the drained pipeline stages
+  uint32_t barrier_offset;  // mbarriers, bytes from the aligned base
+  unsigned int flags;       // glq_flags
 };
+
+// Owner rank of 4-column group g when G groups are dealt to S ranks as
+// [r*G/S, (r+1)*G/S).
+__device__ __forceinline__ int group_owner(int g, int groups, int split) {
+  return ((g + 1) * split + groups - 1) / groups - 1;
+}
 
 template <typename T, int BT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -114,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_dyn + pad;
   const uint32_t sbase = raw_base + pad;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBodyBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + args.barrier_offset);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_slot = reinterpret_cast<int*>(tmem_slot + 2);
@@ -137,6 +154,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 1;
   };
 
+  // ---- TMA producer state (thread 0): W streamed once (evict-first), A reused (evict-last).
+  uint64_t pol_w = 0, pol_a = 0;
+  int issued = 0;
+  // Stage i: one expect_tx for the whole stage, then the W tile and the A tile.
+  auto issue_w = [&](int i) {
+    const int stage = i % kStages;
+    const uint32_t w_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
+    ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
+    ptx::tma_load_2d(w_dst, &tmap_w, (kb_begin + i) * kTileK, tile_n * kTileN, full_bar(stage), pol_w);
+  };
+  auto issue_a = [&](int i) {
+    const int stage = i % kStages;
+    const uint32_t a_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes + kWTileBytes;
+    ptx::tma_load_2d(a_dst, &tmap_a, (kb_begin + i) * kTileK, tile_t * BT, full_bar(stage), pol_a);
+  };
+  auto issue = [&](int i) {
+    issue_w(i);
+    issue_a(i);
+  };
+
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       ptx::mbar_init(full_bar(i), 1);
@@ -144,10 +181,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::mbar_init(done_bar, 1);
     *abort_flag = 0;
-    *issued_slot = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tensormap(&tmap_w);
     ptx::prefetch_tensormap(&tmap_a);
+    pol_w = ptx::policy_evict_first();
+    pol_a = ptx::policy_evict_last();
+    // Start the stream before anything else: the first kStages stages are
+    // free, so these loads need no wait.  With programmatic dependent launch
+    // the predecessor kernel may still be running: A (and W unless the
+    // caller declared the weights static) is read only after the dependency
+    // wait.
+    const int first = nkb < kStages ? nkb : kStages;
+    const bool static_w = (args.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
+    if (static_w) {
+      for (int i = 0; i < first; ++i) issue_w(i);
+    }
+    ptx::grid_dependency_wait();
+    for (; issued < first; ++issued) {
+      if (!static_w) issue_w(issued);
+      issue_a(issued);
+    }
+    *issued_slot = issued;
   }
   if (warp == 1) {
     ptx::tmem_alloc(ptx::smem_addr(tmem_slot), Cfg::kTmemCols);
@@ -157,27 +211,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after_sync();
   const uint32_t tmem_d = *tmem_slot;
+  // Every thread orders its own global accesses after the predecessor grid
+  // (immediate once thread 0 has passed it), then lets the next grid launch.
+  ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
+  const bool recv_dedicated = split > 1 && !args.recv_overlaps;
+  // Split-phase cluster barrier: every thread has started; the matching wait
+  // comes right before the first remote store.
+  if (recv_dedicated) ptx::cluster_arrive_relaxed();
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- TMA producer: W streamed once (evict-first), A reused (evict-last).
-      const uint64_t pol_w = ptx::policy_evict_first();
-      const uint64_t pol_a = ptx::policy_evict_last();
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
+      for (int i = issued; i < nkb; ++i) {
         const int stage = i % kStages;
         const uint32_t round = static_cast<uint32_t>(i / kStages);
-        if (round > 0 &&
-            !ptx::mbar_wait_bounded(empty_bar(stage), (round - 1u) & 1u, abort_flag, kWaitBudgetNs)) {
+        if (!ptx::mbar_wait_bounded(empty_bar(stage), (round - 1u) & 1u, abort_flag, kWaitBudgetNs)) {
           raise(kErrTimeoutProducer);
           break;
         }
-        const uint32_t w_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
-        const uint32_t a_dst = w_dst + kWTileBytes;
-        ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
-        const int kx = (kb_begin + i) * kTileK;
-        ptx::tma_load_2d(w_dst, &tmap_w, kx, tile_n * kTileN, full_bar(stage), pol_w);
-        ptx::tma_load_2d(a_dst, &tmap_a, kx, tile_t * BT, full_bar(stage), pol_a);
+        issue(i);
         issued = i + 1;
       }
       *issued_slot = issued;
@@ -211,7 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncwarp();
 
-  // ---- Epilogue: all 128 threads; thread t owns TMEM lane t = W row t.
+  // ---- Epilogue: 8 warps.  Warp w reads TMEM lanes 32*(w%4).. (W rows) and
+  // every other 8-column chunk (tokens), starting at chunk w/4.
   if (!ptx::mbar_wait_bounded(done_bar, 0u, abort_flag, kWaitBudgetNs)) {
     raise(kErrTimeoutEpilogue);
   }
@@ -219,27 +272,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool aborted = *abort_flag != 0;
   ptx::tc_fence_after_sync();
 
-  const int n_local = warp * 32 + lane;
+  const int lane_group = warp & 3;
+  const int half = warp >> 2;
+  const int n_local = lane_group * 32 + lane;
   const long long n = static_cast<long long>(tile_n) * kTileN + n_local;
   const long long m0 = static_cast<long long>(tile_t) * BT;
   const int mr = static_cast<int>(min(static_cast<long long>(BT), args.m - m0));
+  const int chunks = (mr + 7) >> 3;
   const bool n_ok = n < args.n;
   float bias_v = 0.0f;
   if (args.epilogue != GLQ_EPILOGUE_NONE && n_ok) {
     bias_v = Elem<T>::to_f(static_cast<const T*>(args.bias)[n]);
   }
   T* y = static_cast<T*>(args.y);
-  const uint32_t t_row = tmem_d + (static_cast<uint32_t>(warp * 32) << 16);
+  const uint32_t t_row = tmem_d + (static_cast<uint32_t>(lane_group * 32) << 16);
 
   if (split == 1) {
     if (!aborted) {
-      for (int c0 = 0; c0 < mr; c0 += 16) {
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(c0), r);
+      for (int q = half; q < chunks; q += 2) {
+        uint32_t r[8];
+        ptx::tmem_ld_32x32b_x8(t_row + static_cast<uint32_t>(q * 8), r);
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int mm = c0 + j;
+        for (int j = 0; j < 8; ++j) {
+          const int mm = q * 8 + j;
           if (mm < mr && n_ok) {
             y[(m0 + mm) * args.ldy + n] =
                 Elem<T>::from_f(apply_epilogue(__uint_as_float(r[j]), bias_v, args.epilogue));
@@ -248,48 +304,80 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Partial tile staged as xchg[token][row] (FP32) over the drained pipeline.
-    float* xchg = reinterpret_cast<float*>(smem);
+    // Split-K merge.  Token columns form G groups of 4; rank r owns groups
+    // [r*G/S, (r+1)*G/S).  Every CTA pushes each group of its FP32 partial to
+    // the owner's receive buffer recv[src][row][group] with 16-byte DSMEM
+    // stores; after one cluster barrier each owner sums the S partials of its
+    // groups in split order 0..S-1 from its own shared memory.
+    const int groups = (mr + 3) >> 2;
+    const uint32_t pitch4 = args.recv_pitch4;
+    const uint32_t recv = sbase + args.recv_offset;
+    if (recv_dedicated) {
+      ptx::cluster_wait();  // all CTAs of the cluster are running
+    } else {
+      ptx::cluster_sync();  // all CTAs have drained the pipeline the buffer reuses
+    }
     if (!aborted) {
-      for (int c0 = 0; c0 < mr; c0 += 16) {
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(c0), r);
+      for (int q = half; q < chunks; q += 2) {
+        uint32_t r[8];
+        ptx::tmem_ld_32x32b_x8(t_row + static_cast<uint32_t>(q * 8), r);
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int mm = c0 + j;
-          if (mm < mr) {
-            const float v = __uint_as_float(r[j]);
-            xchg[mm * kTileN + n_local] = v;
-            if (args.partial != nullptr && n_ok) {
-              args.partial[(static_cast<long long>(s) * args.m + m0 + mm) * args.n + n] = v;
+        for (int h = 0; h < 2; ++h) {
+          const int g = 2 * q + h;
+          if (g < groups) {
+            const int owner = group_owner(g, groups, split);
+            const int g_lo = (owner * groups) / split;
+            const uint32_t local =
+                recv + ((static_cast<uint32_t>(s) * kTileN + n_local) * pitch4 + (g - g_lo)) * 16u;
+            ptx::st_dsmem_v4(ptx::map_to_rank(local, static_cast<uint32_t>(owner)),
+                             __uint_as_float(r[4 * h]), __uint_as_float(r[4 * h + 1]),
+                             __uint_as_float(r[4 * h + 2]), __uint_as_float(r[4 * h + 3]));
+          }
+        }
+        if (args.partial != nullptr && n_ok) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int mm = q * 8 + j;
+            if (mm < mr) {
+              args.partial[(static_cast<long long>(s) * args.m + m0 + mm) * args.n + n] =
+                  __uint_as_float(r[j]);
             }
           }
         }
       }
     }
-    ptx::cluster_sync();
+    ptx::cluster_sync();  // every push into this CTA is complete and visible
     if (!aborted) {
-      const int m_lo = (s * mr) / split;
-      const int m_hi = ((s + 1) * mr) / split;
-      for (int mm = m_lo; mm < m_hi; ++mm) {
-        const uint32_t local = ptx::smem_addr(&xchg[mm * kTileN + n_local]);
-        float acc = 0.0f;
-        for (int r = 0; r < split; ++r) {
-          acc += ptx::ld_dsmem_f32(ptx::map_to_rank(local, static_cast<uint32_t>(r)));
+      const int g_lo = (s * groups) / split;
+      const int g_hi = ((s + 1) * groups) / split;
+      const float4* rv = reinterpret_cast<const float4*>(smem + args.recv_offset);
+      for (int j = half; j < g_hi - g_lo; j += 2) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int src = 0; src < split; ++src) {
+          const float4 v = rv[(src * kTileN + n_local) * pitch4 + j];
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
         }
-        if (n_ok) {
-          y[(m0 + mm) * args.ldy + n] = Elem<T>::from_f(apply_epilogue(acc, bias_v, args.epilogue));
+        const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+        const int mm0 = 4 * (g_lo + j);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int mm = mm0 + c;
+          if (mm < mr && n_ok) {
+            y[(m0 + mm) * args.ldy + n] = Elem<T>::from_f(apply_epilogue(vals[c], bias_v, args.epilogue));
+          }
         }
       }
     }
-    ptx::cluster_sync();  // peers have finished reading this CTA's partials
   }
 
   // ---- Teardown: after an abort, let this CTA's own TMA loads land first.
-  if (aborted && warp == 0 && lane == 0) {
-    const int issued = *issued_slot;
-    for (int i = max(0, issued - kStages); i < issued; ++i) {
+  if (aborted && threadIdx.x == 0) {
+    const int done_issue = *issued_slot;
+    for (int i = max(0, done_issue - kStages); i < done_issue; ++i) {
       if (!ptx::mbar_wait_bounded(full_bar(i % kStages), static_cast<uint32_t>(i / kStages) & 1u,
                                   nullptr, kWaitBudgetNs)) {
         atomicOr(args.err, kErrTimeoutDrain);
@@ -341,7 +429,7 @@ bool encode_kmajor(CUtensorMap* map, CUtensorMapDataType type, const void* base,
 template <typename T, int BT>
 cudaError_t set_attrs() {
   return cudaFuncSetAttribute(tc_linear_kernel<T, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              TcConfig<BT>::kSmemBytes);
+                              static_cast<int>(kSmemLimit));
 }
 
 template <typename T>
@@ -365,6 +453,7 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
       !encode_kmajor(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, BT)) {
     return cudaErrorInvalidValue;
   }
+  using Cfg = TcConfig<BT>;
   TcArgs args;
   args.m = static_cast<int>(p.m);
   args.n = static_cast<int>(p.n);
@@ -377,20 +466,41 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   args.ldy = p.ldy;
   args.partial = p.partial;
   args.err = err;
+  args.flags = p.flags;
+  // Shared memory: [pipeline stages][split-K receive buffer][mbarriers].
+  // The receive buffer gets its own region when it fits, otherwise it reuses
+  // the drained stages (one more cluster barrier).
+  uint32_t recv_bytes = 0, pitch4 = 1;
+  if (split > 1) {
+    const uint32_t groups = BT / 4;
+    const uint32_t width = (groups + split - 1) / split;
+    pitch4 = (width % 2 == 0) ? width + 1 : width;
+    recv_bytes = static_cast<uint32_t>(split) * kTileN * pitch4 * 16u;
+  }
+  const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= kSmemLimit;
+  args.recv_offset = dedicated ? Cfg::kPipeBytes : 0;
+  args.recv_pitch4 = pitch4;
+  args.recv_overlaps = dedicated ? 0 : 1;
+  const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : (Cfg::kPipeBytes > recv_bytes ? Cfg::kPipeBytes : recv_bytes);
+  args.barrier_offset = (body + 15u) & ~15u;
+  const uint32_t smem_bytes = 1024 + args.barrier_offset + Cfg::kBarrierBytes;
+  if (smem_bytes > kSmemLimit) return cudaErrorInvalidValue;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>((p.n + kTileN - 1) / kTileN),
                      static_cast<unsigned>((p.m + BT - 1) / BT));
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = TcConfig<BT>::kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(split);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
   return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT>, tmap_w, tmap_a, args);
 }
 

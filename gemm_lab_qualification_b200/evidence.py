@@ -6,11 +6,12 @@
   (evidence.py:87-105): per round a fresh shuffle of the functions, each
   timed over ``inner`` back-to-back calls.  With two functions this is the
   randomised AB/BA pair protocol.
-* ``device_measure`` -- per-call device time without host dispatch gaps:
-  each round first enqueues a short GPU hold (``torch.cuda._sleep``), then
-  every function bracketed by its own pair of CUDA events, so all launches
-  are queued before the GPU reaches them and each event pair spans exactly
-  one call's device work.  Order is reshuffled every round.
+* ``device_measure`` -- the same event protocol without host dispatch gaps:
+  each sample first enqueues a short GPU hold (``torch.cuda._sleep``) so the
+  ``inner`` launches behind it are all queued before the GPU reaches them;
+  the event pair then spans exactly ``inner`` back-to-back calls of device
+  work.  ``inner = 1`` gives the isolated single-call latency, which also
+  contains the device-side launch latency of that one kernel.
 """
 from __future__ import annotations
 
@@ -66,29 +67,33 @@ def hold_cycles(microseconds: float) -> int:
     return int(microseconds * 1965)
 
 
-def device_measure(functions: dict[str, Callable[[], object]], rounds: int, seed: int = 7,
-                   hold_us: float = 300.0, stream=None) -> dict[str, list[float]]:
+def device_measure(functions: dict[str, Callable[[], object]], rounds: int, inner: int = 10, seed: int = 7,
+                   hold_us: float = 400.0) -> dict[str, list[float]]:
     """Per-call device milliseconds, ``rounds`` samples per function.
 
-    Each round: synchronize, a GPU hold of ``hold_us``, then every function
-    (shuffled) between its own two events on ``stream``.  Returns raw samples.
+    Each sample: a GPU hold of ``hold_us`` (so the launches behind it queue
+    up), a start event, ``inner`` back-to-back calls, an end event, all on the
+    current stream; the sample is the span / ``inner``.  Functions are visited
+    in a fresh shuffled order every round.  Returns the raw samples.
     """
     import torch
-    stream = stream or torch.cuda.current_stream()
+    stream = torch.cuda.current_stream()
     rng = random.Random(seed)
     raw = {k: [] for k in functions}
     keys = list(functions)
     events = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for k in keys}
     for _ in range(rounds):
         rng.shuffle(keys)
-        torch.cuda._sleep(hold_cycles(hold_us))
         for key in keys:
             start, end = events[key]
+            torch.cuda._sleep(hold_cycles(hold_us))
             start.record(stream)
-            functions[key]()
+            fn = functions[key]
+            for _ in range(inner):
+                fn()
             end.record(stream)
         stream.synchronize()
         for key in keys:
             start, end = events[key]
-            raw[key].append(start.elapsed_time(end))
+            raw[key].append(start.elapsed_time(end) / inner)
     return raw

@@ -14,6 +14,11 @@ violations, with every Triton body replaced by one call through the C ABI
   ``adaptive_*`` names keep their signatures but always run the native
   kernels; the ``*_path`` helpers report the native path name.
 * Every call records the GPU path it took; ``last_path()`` returns it.
+* ``launch_options(pdl=..., static_weights=...)`` sets per-thread launch
+  flags: programmatic dependent launch (on by default; stream semantics
+  unchanged) and the opt-in declaration that the weight operand is not
+  written by the preceding kernel, which lets a call start streaming it
+  before its predecessor finishes.
 
 Cited reference lines are in ``kernels.py`` of the reference project.
 """
@@ -31,10 +36,37 @@ __all__ = [
     "adaptive_bias_silu_path", "adaptive_bias_silu",
     "triton_splitk_matmul_into", "triton_splitk_matmul", "TritonSplitKPlan",
     "AdaptiveMatmulPlan", "TritonAdaptivePlan", "adaptive_path", "triton_adaptive_matmul",
-    "linear_into", "last_path", "planned_path",
+    "linear_into", "last_path", "planned_path", "launch_options",
 ]
 
 _last = threading.local()
+_options = threading.local()
+
+
+class launch_options:
+    """Per-thread launch flags for the native calls made inside the block.
+
+    pdl: launch with programmatic dependent launch (default True).
+    static_weights: the ``b`` operand is not written by the kernel that
+    precedes each call in its stream (inference weights); the kernels then
+    request it before waiting for that kernel (default False).
+    """
+
+    def __init__(self, pdl: bool = True, static_weights: bool = False) -> None:
+        self.flags = (0 if pdl else _native.FLAG_NO_PDL) | (_native.FLAG_STATIC_WEIGHTS if static_weights else 0)
+        self._saved = 0
+
+    def __enter__(self) -> "launch_options":
+        self._saved = getattr(_options, "flags", 0)
+        _options.flags = self.flags
+        return self
+
+    def __exit__(self, *exc) -> None:
+        _options.flags = self._saved
+
+
+def _flags() -> int:
+    return getattr(_options, "flags", 0)
 
 
 def last_path() -> tuple[str, int] | None:
@@ -90,7 +122,7 @@ def linear_into(a: torch.Tensor, b: torch.Tensor, output: torch.Tensor, bias: to
         _validate_bias(bias, a, n)
     epilogue = (_native.EPILOGUE_NONE if bias is None else
                 _native.EPILOGUE_BIAS_SILU if activation == "silu" else _native.EPILOGUE_BIAS)
-    _record(_native.linear(a, b, output, bias, epilogue, split_k, partial))
+    _record(_native.linear(a, b, output, bias, epilogue, split_k, partial, flags=_flags()))
     return output
 
 
@@ -107,7 +139,7 @@ def planned_path(a: torch.Tensor, b: torch.Tensor, split_k: int = 0) -> tuple[st
 def triton_matmul_into(a: torch.Tensor, b: torch.Tensor, output: torch.Tensor) -> torch.Tensor:
     m, n, _ = _validate_inputs(a, b, "triton_matmul")
     _validate_output(output, a, m, n)
-    _record(_native.linear(a, b, output))
+    _record(_native.linear(a, b, output, flags=_flags()))
     return output
 
 
@@ -135,7 +167,7 @@ def triton_bias_silu_into(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor,
     m, n, _ = _validate_inputs(a, b, "triton_bias_silu")
     _validate_bias(bias, a, n)
     _validate_output(output, a, m, n)
-    _record(_native.linear(a, b, output, bias, _native.EPILOGUE_BIAS_SILU))
+    _record(_native.linear(a, b, output, bias, _native.EPILOGUE_BIAS_SILU, flags=_flags()))
     return output
 
 
@@ -186,7 +218,7 @@ def triton_splitk_matmul_into(a: torch.Tensor, b: torch.Tensor, partial: torch.T
     if not partial.is_contiguous():
         raise ValueError("partial tensor must be contiguous")
     _validate_output(output, a, m, n)
-    _record(_native.linear(a, b, output, None, _native.EPILOGUE_NONE, split_k, partial))
+    _record(_native.linear(a, b, output, None, _native.EPILOGUE_NONE, split_k, partial, flags=_flags()))
     return output
 
 

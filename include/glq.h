@@ -88,6 +88,21 @@ enum glq_status {
 
 #define GLQ_MAX_SPLIT 8
 
+/* Per-call flags of glq_linear_ex (bitwise OR). */
+enum glq_flags {
+  /* Launch without programmatic dependent launch.  By default the tcgen05
+   * and GEMV kernels are launched with it: a kernel lets the next kernel of
+   * the stream begin launching early, and every kernel waits for its
+   * predecessor to complete (griddepcontrol.wait) before it touches global
+   * memory, so stream order semantics are unchanged. */
+  GLQ_FLAG_NO_PDL = 1u << 0,
+  /* The weight operand B is not written by the kernel that precedes this call
+   * in the stream (true for inference weights).  The kernel then starts
+   * streaming B before the dependency wait, overlapping the predecessor's
+   * tail.  Only A, bias and Y wait for the predecessor. */
+  GLQ_FLAG_STATIC_WEIGHTS = 1u << 1
+};
+
 /*
  * glq_linear -- the one general entry point.
  *
@@ -117,6 +132,20 @@ int glq_linear(int dtype,
                int64_t M, int64_t N, int64_t K,
                int split_k, void* workspace, size_t workspace_bytes,
                void* stream, int* path_out, int* split_out);
+
+/*
+ * glq_linear_ex -- glq_linear with per-call flags (enum glq_flags).
+ * glq_linear(...) == glq_linear_ex(..., 0).  No reference counterpart: the
+ * reference's launches have no dependency control.
+ */
+int glq_linear_ex(int dtype,
+                  const void* A, int64_t a_row_stride, int64_t a_col_stride,
+                  const void* B, int64_t b_k_stride, int64_t b_n_stride,
+                  const void* bias, int epilogue,
+                  void* Y, int64_t y_row_stride,
+                  int64_t M, int64_t N, int64_t K,
+                  int split_k, void* workspace, size_t workspace_bytes,
+                  void* stream, unsigned int flags, int* path_out, int* split_out);
 
 /*
  * glq_linear_f16 -- FP16 form with the argument order of the lab's proposed

@@ -148,6 +148,9 @@ def test_linear_validation_precedes_device_use():
     assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 1, 1, 1, 9, None, 0, None, None, None) == 3
     assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, -1, 1, 1, 0, None, 0, None, None, None) == 2
     assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 1, 1, 1, 0, None, 0, None, None, None) == 1
+    # unknown flag bits
+    assert lib.glq_linear_ex(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 1, 1, 1, 0, None, 0, None, 1 << 7,
+                             None, None) == 1
     # bias+SiLU without a bias pointer
     assert lib.glq_linear(0, 16, 1, 1, 16, 1, 1, None, 2, 16, 1, 1, 1, 1, 0, None, 0, None, None, None) == 1
     # empty problems succeed without touching a device and report "empty"

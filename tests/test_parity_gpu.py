@@ -295,3 +295,41 @@ def test_bias_only_epilogue_and_streams(cuda_device):
     stream.synchronize()
     expected = oracle.linear_reference(a, w) + bias.double().numpy()[None, :]
     oracle.compare(host(out), expected, U_ATOL, U_RTOL)
+
+
+@pytest.mark.parametrize("m", [1, 32])
+def test_launch_modes_bitwise_identical(cuda_device, m):
+    """PDL on/off and the static-weights flag change scheduling, never results."""
+    a, w, bias = workloads.uniform_inputs(m, 4096, 4096)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    outs = []
+    for opts in (dict(pdl=False), dict(), dict(static_weights=True)):
+        with kernels.launch_options(**opts):
+            # back-to-back calls so dependent launches really overlap
+            for _ in range(4):
+                out = kernels.triton_bias_silu(da, dw.t(), db)
+        outs.append(out)
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
+    oracle.compare(host(outs[0]), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+
+
+def test_pdl_chain_respects_dependencies(cuda_device):
+    """y1 = f(A, W1) feeds the next call as its A; with PDL the second call
+    must still see the finished y1 (griddepcontrol.wait before reading A)."""
+    a, w1, b1 = workloads.uniform_inputs(32, 4096, 4096)
+    _, w2, b2 = workloads.uniform_inputs(32, 4096, 4096, seed=8)
+    da, dw1, db1, dw2, db2 = (t.to(cuda_device) for t in (a, w1, b1, w2, b2))
+    with kernels.launch_options(static_weights=True):
+        y1 = kernels.triton_bias_silu(da, dw1.t(), db1)
+        y2 = kernels.triton_bias_silu(y1, dw2.t(), db2)
+    torch.cuda.synchronize()
+    ref1 = kernels.triton_bias_silu(da, dw1.t(), db1)
+    with kernels.launch_options(pdl=False):
+        ref2 = kernels.triton_bias_silu(ref1, dw2.t(), db2)
+    torch.cuda.synchronize()
+    assert torch.equal(y1.view(torch.int16), ref1.view(torch.int16))
+    assert torch.equal(y2.view(torch.int16), ref2.view(torch.int16))
+    expected = oracle.linear_reference(host(y1).astype(np.float16), w2, b2, silu=True)
+    oracle.compare(host(y2), expected, U_ATOL, U_RTOL)
