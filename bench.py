@@ -278,6 +278,24 @@ def single_gpu(args, torch, dev) -> dict:
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     isolated = device_measure(fns, rounds=max(10, args.steps // 4), inner=1)
+    # Same-round vendor comparator, same protocol and rotating W copies:
+    # cuBLASLt through torch (F.linear = GEMM with the bias epilogue, then a
+    # separate SiLU kernel: equal semantics except that the bias epilogue
+    # rounds to FP16 before the SiLU) and the plain GEMM (torch.mm).
+    def vendor(m, variant):
+        st = state[m]
+
+        def run():
+            w = st["w"][st["i"] % copies]
+            st["i"] += 1
+            if variant == "fused":
+                torch.nn.functional.silu(torch.nn.functional.linear(st["a"], w, st["bias"]), inplace=True)
+            else:
+                torch.mm(st["a"], w.t(), out=st["plain"])
+        return run
+
+    cublas = device_measure({f"{v}/m{m}": vendor(m, v) for m in sweep_m for v in ("fused", "plain")},
+                            rounds=max(10, args.steps // 3), inner=args.inner)
     # Launch modes of the fused calls: without programmatic dependent launch,
     # and with the inference declaration that W is static.
     modes = {}
@@ -312,6 +330,8 @@ def single_gpu(args, torch, dev) -> dict:
             row[f"{v}_isolated_p50_us"] = statistics.median(isolated[f"{v}/m{m}"]) * 1e3
         for label, samples in modes.items():
             row[f"fused_{label}_p50_us"] = statistics.median(samples[f"fused/m{m}"]) * 1e3
+        for v in ("fused", "plain"):
+            row[f"cublas_{v}_p50_us"] = statistics.median(cublas[f"{v}/m{m}"]) * 1e3
         sweep[str(m)] = row
 
     head = sweep[str(args.m)]

@@ -71,7 +71,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int auto_split(int64_t tiles, int64_t k_blocks, int sm_count) {
   int64_t s = sm_count / std::max<int64_t>(tiles, 1);
-  s = std::min<int64_t>(s, GLQ_MAX_SPLIT);
+  s = std::min<int64_t>(s, kMaxAutoSplit);
   s = std::min<int64_t>(s, k_blocks);
   // Each split keeps at least two K blocks so the pipeline has depth.
   while (s > 1 && k_blocks / s < 2) --s;
@@ -92,6 +92,7 @@ int validate(int dtype, int epilogue, int64_t m, int64_t n, int64_t k, int split
 int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->split = 1;
   c->tile_t = 0;
+  c->tile_n = 128;
   if (p.m == 0 || p.n == 0) {
     c->path = GLQ_PATH_EMPTY;
     c->kernel = kKernelNone;
@@ -126,11 +127,15 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   }
   c->kernel = kKernelTc;
   c->tile_t = tc_token_tile(p.m);
+  c->tile_n = tc_tile_rows(p.m, p.n);
   const int64_t k_blocks = tc_k_blocks(p.k);
-  const int64_t tiles = ((p.n + 127) / 128) * ((p.m + c->tile_t - 1) / c->tile_t);
+  const int64_t tiles = ((p.n + c->tile_n - 1) / c->tile_n) * ((p.m + c->tile_t - 1) / c->tile_t);
   int s = split_k > 0 ? split_k : auto_split(tiles, k_blocks, sm_count > 0 ? sm_count : 148);
   s = static_cast<int>(std::min<int64_t>(s, k_blocks));
   c->split = std::max(s, 1);
+  // Split-K tiles hold at most 128 tokens (the merge buffers must fit in the
+  // drained pipeline memory).
+  if (c->split > 1 && c->tile_t > 128) c->tile_t = 128;
   if (p.n % 128 != 0 || p.k % 64 != 0) {
     c->path = GLQ_PATH_TAIL;
   } else {
@@ -233,7 +238,7 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
     case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
-    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, dev->error_word, s); break;
+    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, dev->error_word, s); break;
     case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
     default: break;
   }
@@ -276,7 +281,8 @@ size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k) {
   } else {
     const int64_t kb = glq::tc_k_blocks(K);
     const int bt = glq::tc_token_tile(M);
-    const int64_t tiles = ((N + 127) / 128) * ((M + bt - 1) / bt);
+    const int tn = glq::tc_tile_rows(M, N);
+    const int64_t tiles = ((N + tn - 1) / tn) * ((M + bt - 1) / bt);
     s = split_k > 0 ? split_k : glq::auto_split(tiles, kb, 148);
     s = static_cast<int>(std::min<int64_t>(s, kb));
   }

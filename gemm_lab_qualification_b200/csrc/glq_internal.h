@@ -47,6 +47,7 @@ struct Choice {
   int split;    // K ranges merged in-kernel (1 = none)
   int kernel;   // Kernel below
   int tile_t;   // token tile (MMA N) of the tcgen05 kernel
+  int tile_n;   // W rows per CTA of the tcgen05 kernel (128 or 256)
 };
 
 enum Kernel : int {
@@ -63,6 +64,16 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* out);
 // Number of 64-wide K blocks of the tcgen05 kernel.
 inline int64_t tc_k_blocks(int64_t k) { return (k + 63) / 64; }
 
+// W rows per CTA of the tcgen05 kernel: 256-row tiles (32 KB TMA boxes) for
+// small token tiles when the layer is wide enough to fill the device with at
+// most 4-way split-K (N >= 8192), 128 otherwise.
+inline int tc_tile_rows(int64_t m, int64_t n) { return (m <= 32 && n >= 8192) ? 256 : 128; }
+
+// Largest automatic split-K: clusters of up to 4 CTAs with ~200 KB of shared
+// memory each still pack one wave onto the 148 SMs (33 clusters of 4 are
+// co-resident on B200); larger clusters may not, which costs a second wave.
+constexpr int kMaxAutoSplit = 4;
+
 // Token tile of the tcgen05 kernel for m tokens.
 inline int tc_token_tile(int64_t m) {
   if (m <= 16) return 16;
@@ -78,7 +89,7 @@ cudaError_t launch_gemv(const Problem& p, int split, unsigned int* err, cudaStre
 cudaError_t launch_generic(const Problem& p, cudaStream_t s);
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, unsigned int* err, cudaStream_t s);
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, unsigned int* err, cudaStream_t s);
 
 // Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).
 cudaError_t tc_prepare_device();

@@ -239,6 +239,29 @@ __device__ __forceinline__ void st_dsmem_v4(uint32_t cluster_addr, float a, floa
                : "memory");
 }
 
+// Bulk copy (DMA) of `bytes` from this CTA's shared memory to the shared
+// memory of a CTA of the cluster; completes `bytes` on that CTA's mbarrier
+// `remote_bar`.  dst and remote_bar are already mapped to the destination
+// rank; addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                  uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "r"(src), "r"(bytes), "r"(remote_bar)
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory writes before
+// later async-proxy (bulk copy / TMA) accesses of that memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Release-ordered arrive on the cluster barrier (pairs with cluster_wait).
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
 // Programmatic dependent launch: wait until the preceding grid in the stream
 // has completed and its memory is visible (no-op without the launch
 // attribute), and allow the next grid to begin launching.

@@ -7,19 +7,21 @@
 // Design (swap-AB, decode shapes are weight-bandwidth bound):
 //   * W rows fill the 128-lane MMA M dimension; the token batch is the MMA N
 //     dimension (16..256), so M = 1..128 tokens cost one W pass.
-//   * One CTA = 256 threads owns a 128-row W tile x a token tile x one
-//     contiguous range of 64-wide K blocks.  Thread 0 starts the TMA stream
+//   * One CTA = 256 threads owns a 128- or 256-row W tile (one M = 128 MMA
+//     and TMEM accumulator per 128 rows) x a token tile x one contiguous
+//     range of 64-wide K blocks.  Thread 0 starts the TMA stream
 //     (128-byte swizzle, K-major) into a STAGES-deep mbarrier ring before
 //     anything else; warp 1 allocates TMEM and lane 0 issues tcgen05.mma; all
 //     eight warps run the epilogue from TMEM (lane = W row, column = token),
 //     two warps per 32-lane TMEM quarter splitting the token columns.
 //   * Split-K: the K ranges of one tile are the CTAs of one thread-block
-//     cluster.  After the main loop every CTA pushes each 4-token group of
-//     its FP32 partial tile to the CTA that owns the group (16-byte DSMEM
-//     stores, no round trip); after one cluster barrier each owner sums the S
-//     partials of its groups in split order 0..S-1 from its own shared
-//     memory, applies bias + SiLU and stores.  The merge order is fixed, so
-//     results are bitwise reproducible, and nothing waits on a flag.
+//     cluster.  After the main loop every CTA stages its FP32 partial tile in
+//     its drained pipeline memory and ships each owner's 4-token groups with
+//     one DSMEM bulk copy that completes on the owner's receive mbarrier; the
+//     owner waits only on that barrier, sums the S partials of its groups in
+//     split order 0..S-1 from its own shared memory, applies bias + SiLU and
+//     stores.  The merge order is fixed, so results are bitwise
+//     reproducible, and the only spin-waits are bounded mbarrier waits.
 //   * Programmatic dependent launch: every thread waits for the predecessor
 //     grid (griddepcontrol.wait) before touching global memory and then lets
 //     the next grid launch, so back-to-back calls overlap launch latency,
@@ -29,7 +31,7 @@
 //   * Every mbarrier wait is bounded (glq_ptx.cuh); on expiry the CTA raises
 //     a bit in the device error word, stops issuing work, drains its own
 //     in-flight TMA loads (bounded), still takes part in both cluster
-//     barriers, frees TMEM and returns.
+//     barrier phases, frees TMEM and returns.
 //
 // Reference counterpart: ptx_mma_pipelined_kernel<..., SPLIT_K> +
 // ptx_mma_splitk_reduce_kernel (csrc/ptx_mma.cuh:502-770, 851-868) and the
@@ -76,21 +78,28 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilo
   return __fdividef(v, 1.0f + __expf(-v));  // SiLU = v * sigmoid(v)
 }
 
-constexpr int kTileN = 128;  // W rows per CTA (MMA M, TMEM lanes)
-constexpr int kTileK = 64;   // K elements per stage: one 128-byte swizzle row
+constexpr int kTileK = 64;  // K elements per stage: one 128-byte swizzle row
 constexpr int kThreads = 256;
-constexpr uint32_t kWTileBytes = kTileN * kTileK * 2;
 constexpr uint32_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
 
-template <int BT>
+// BT: token tile (MMA N).  TN: W rows per CTA, one M = 128 MMA (and one TMEM
+// accumulator of BT columns) per 128 rows.  A 256-row tile moves W in 32 KB
+// TMA boxes, which streams HBM measurably better than 16 KB boxes at equal
+// bytes in flight; it is used for small token tiles.
+template <int BT, int TN>
 struct TcConfig {
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128 is 16..256 step 16");
+  static_assert(TN == 128 || TN == 256, "tile rows are one or two M=128 MMAs");
+  static constexpr int kAcc = TN / 128;
+  static constexpr uint32_t kWTileBytes = TN * kTileK * 2;
   static constexpr uint32_t kATileBytes = BT * kTileK * 2;
   static constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
-  static constexpr int kStages = BT <= 64 ? 8 : (BT <= 128 ? 6 : 4);
-  static constexpr uint32_t kTmemCols = BT < 32 ? 32 : BT;
+  static constexpr int kStages = TN == 256 ? 4 : (BT <= 64 ? 8 : (BT <= 128 ? 6 : 4));
+  static constexpr uint32_t kAccCols = kAcc * BT;
+  static constexpr uint32_t kTmemCols =
+      kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
   static constexpr uint32_t kPipeBytes = kStages * kStageBytes;
-  static constexpr uint32_t kBarrierBytes = (2 * kStages + 1) * 8 + 16;
+  static constexpr uint32_t kBarrierBytes = (2 * kStages + 2) * 8 + 16;
   static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-B aligned");
   static_assert(1024 + kPipeBytes + kBarrierBytes <= kSmemLimit, "pipeline exceeds shared memory");
 };
@@ -106,8 +115,8 @@ struct TcArgs {
   float* partial;
   unsigned int* err;
   uint32_t recv_offset;     // split-K receive buffer, bytes from the 1024-aligned base
-  uint32_t recv_pitch4;     // its row pitch in 16-byte units (odd: conflict-free v4 stores)
-  int recv_overlaps;        // 1: it reuses the drained pipeline stages
+  uint32_t stage_offset;    // split-K send staging buffer (inside the drained pipeline)
+  int recv_overlaps;        // 1: the receive buffer reuses the drained pipeline stages
   uint32_t barrier_offset;  // mbarriers, bytes from the aligned base
   unsigned int flags;       // glq_flags
 };
@@ -118,11 +127,12 @@ __device__ __forceinline__ int group_owner(int g, int groups, int split) {
   return ((g + 1) * split + groups - 1) / groups - 1;
 }
 
-template <typename T, int BT>
+template <typename T, int BT, int TN>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_a, const TcArgs args) {
-  using Cfg = TcConfig<BT>;
+  using Cfg = TcConfig<BT, TN>;
+  constexpr uint32_t kWTileBytes = Cfg::kWTileBytes;
   constexpr int kStages = Cfg::kStages;
 
   extern __shared__ uint8_t smem_dyn[];
@@ -132,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = raw_base + pad;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + args.barrier_offset);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_slot = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -149,6 +159,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto full_bar = [&](int i) { return ptx::smem_addr(&bars[i]); };
   auto empty_bar = [&](int i) { return ptx::smem_addr(&bars[kStages + i]); };
   const uint32_t done_bar = ptx::smem_addr(&bars[2 * kStages]);
+  const uint32_t recv_bar = ptx::smem_addr(&bars[2 * kStages + 1]);
+
+  // Token columns of this tile and, for split-K, the 4-column groups this
+  // CTA owns: groups are dealt to the S ranks as [r*G/S, (r+1)*G/S).
+  const long long m0 = static_cast<long long>(tile_t) * BT;
+  const int mr = static_cast<int>(min(static_cast<long long>(BT), args.m - m0));
+  const int groups = (mr + 3) >> 2;
+  const int own_lo = (s * groups) / split;
+  const int own_hi = ((s + 1) * groups) / split;
+  const int own_width = own_hi - own_lo;
   auto raise = [&](unsigned int bit) {
     atomicOr(args.err, bit);
     *abort_flag = 1;
@@ -162,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int stage = i % kStages;
     const uint32_t w_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
     ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
-    ptx::tma_load_2d(w_dst, &tmap_w, (kb_begin + i) * kTileK, tile_n * kTileN, full_bar(stage), pol_w);
+    ptx::tma_load_2d(w_dst, &tmap_w, (kb_begin + i) * kTileK, tile_n * TN, full_bar(stage), pol_w);
   };
   auto issue_a = [&](int i) {
     const int stage = i % kStages;
@@ -180,8 +200,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(empty_bar(i), 1);
     }
     ptx::mbar_init(done_bar, 1);
+    ptx::mbar_init(recv_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
+    // The owner expects one 16-byte store per (source rank, W row, owned group).
+    if (split > 1) {
+      ptx::mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(split) * TN *
+                                               static_cast<uint32_t>(own_width) * 16u);
+    }
     ptx::prefetch_tensormap(&tmap_w);
     ptx::prefetch_tensormap(&tmap_a);
     pol_w = ptx::policy_evict_first();
@@ -215,10 +241,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (immediate once thread 0 has passed it), then lets the next grid launch.
   ptx::grid_dependency_wait();
   ptx::grid_launch_dependents();
+
+  // Warp w reads TMEM lanes 32*(w%4)..+31.  With two accumulators warpgroup
+  // h owns accumulator h (W rows 128h..) and all its columns; with one, the
+  // two warpgroups take alternate 16-column chunks of it.
+  const int lane_group = warp & 3;
+  const int half = warp >> 2;
+  const int acc_idx = Cfg::kAcc == 2 ? half : 0;
+  const int q_first = Cfg::kAcc == 2 ? 0 : half;
+  const int q_step = Cfg::kAcc == 2 ? 1 : 2;
+  const int n_local = acc_idx * 128 + lane_group * 32 + lane;  // == threadIdx.x % TN
+  const long long n = static_cast<long long>(tile_n) * TN + n_local;
+  const bool n_ok = n < args.n;
+  float bias_v = 0.0f;
+  if (args.epilogue != GLQ_EPILOGUE_NONE && n_ok) {
+    bias_v = Elem<T>::to_f(static_cast<const T*>(args.bias)[n]);
+  }
+
+  // Cluster barrier phase 1 proves every CTA of the cluster is running (its
+  // receive barrier initialised) before anyone stores into it.  With a
+  // dedicated receive buffer it is armed now and the epilogue warps absorb
+  // the wait during the main loop; when the buffer reuses the pipeline it is
+  // armed only after the main loop.
   const bool recv_dedicated = split > 1 && !args.recv_overlaps;
-  // Split-phase cluster barrier: every thread has started; the matching wait
-  // comes right before the first remote store.
-  if (recv_dedicated) ptx::cluster_arrive_relaxed();
+  if (recv_dedicated) {
+    ptx::cluster_arrive_relaxed();
+    if (warp >= 2) ptx::cluster_wait();
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -236,8 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---- MMA issuer: D[128 x BT] += W_tile[128 x 64] * A_tile[BT x 64]^T.
-      constexpr uint32_t idesc = ptx::umma_idesc_f16(kTileN, BT, Elem<T>::kFormat);
+      // ---- MMA issuer: per 128 W rows h, D_h[128 x BT] += W_h[128 x 64] * A[BT x 64]^T;
+      // accumulator h occupies TMEM columns [h*BT, (h+1)*BT).
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT, Elem<T>::kFormat);
       for (int i = 0; i < nkb; ++i) {
         const int stage = i % kStages;
         const uint32_t round = static_cast<uint32_t>(i / kStages);
@@ -252,9 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kTileK / 16; ++kk) {
           // Each MMA consumes K = 16 (32 bytes); the descriptor start address
-          // is in 16-byte units, so step by 2 inside the swizzled row.
-          ptx::tc_mma_f16(tmem_d, w_desc + 2u * kk, a_desc + 2u * kk, idesc,
-                          (i > 0 || kk > 0) ? 1u : 0u);
+          // is in 16-byte units, so step by 2 inside the swizzled row.  The
+          // 128-row halves of a 256-row W tile are 16 KB (1024 units) apart.
+#pragma unroll
+          for (int h = 0; h < Cfg::kAcc; ++h) {
+            ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT), w_desc + 1024u * h + 2u * kk,
+                            a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         ptx::tc_commit(empty_bar(stage));
       }
@@ -262,9 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncwarp();
+  if (recv_dedicated && warp < 2) ptx::cluster_wait();
 
-  // ---- Epilogue: 8 warps.  Warp w reads TMEM lanes 32*(w%4).. (W rows) and
-  // every other 8-column chunk (tokens), starting at chunk w/4.
+  // ---- Epilogue: 8 warps (rows and chunks as assigned above).
   if (!ptx::mbar_wait_bounded(done_bar, 0u, abort_flag, kWaitBudgetNs)) {
     raise(kErrTimeoutEpilogue);
   }
@@ -272,30 +326,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool aborted = *abort_flag != 0;
   ptx::tc_fence_after_sync();
 
-  const int lane_group = warp & 3;
-  const int half = warp >> 2;
-  const int n_local = lane_group * 32 + lane;
-  const long long n = static_cast<long long>(tile_n) * kTileN + n_local;
-  const long long m0 = static_cast<long long>(tile_t) * BT;
-  const int mr = static_cast<int>(min(static_cast<long long>(BT), args.m - m0));
-  const int chunks = (mr + 7) >> 3;
-  const bool n_ok = n < args.n;
-  float bias_v = 0.0f;
-  if (args.epilogue != GLQ_EPILOGUE_NONE && n_ok) {
-    bias_v = Elem<T>::to_f(static_cast<const T*>(args.bias)[n]);
-  }
+  const int chunks = (mr + 15) >> 4;
   T* y = static_cast<T*>(args.y);
-  const uint32_t t_row = tmem_d + (static_cast<uint32_t>(lane_group * 32) << 16);
+  const uint32_t t_row =
+      tmem_d + (static_cast<uint32_t>(lane_group * 32) << 16) + static_cast<uint32_t>(acc_idx * BT);
 
   if (split == 1) {
     if (!aborted) {
-      for (int q = half; q < chunks; q += 2) {
-        uint32_t r[8];
-        ptx::tmem_ld_32x32b_x8(t_row + static_cast<uint32_t>(q * 8), r);
+      for (int q = q_first; q < chunks; q += q_step) {
+        uint32_t r[16];
+        ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(q * 16), r);
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int mm = q * 8 + j;
+        for (int j = 0; j < 16; ++j) {
+          const int mm = q * 16 + j;
           if (mm < mr && n_ok) {
             y[(m0 + mm) * args.ldy + n] =
                 Elem<T>::from_f(apply_epilogue(__uint_as_float(r[j]), bias_v, args.epilogue));
@@ -304,41 +348,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Split-K merge.  Token columns form G groups of 4; rank r owns groups
-    // [r*G/S, (r+1)*G/S).  Every CTA pushes each group of its FP32 partial to
-    // the owner's receive buffer recv[src][row][group] with 16-byte DSMEM
-    // stores; after one cluster barrier each owner sums the S partials of its
-    // groups in split order 0..S-1 from its own shared memory.
-    const int groups = (mr + 3) >> 2;
-    const uint32_t pitch4 = args.recv_pitch4;
+    // Split-K merge.  Every CTA stages its FP32 partial tile in its own
+    // drained pipeline memory as [group][row] (16 bytes per entry, so
+    // consecutive rows are consecutive: no bank conflicts).  4-token groups
+    // are dealt to the S ranks as [r*G/S, (r+1)*G/S), so the groups of rank r
+    // form one contiguous block; thread 0 ships it to rank r's receive slot
+    // recv[src = this rank] with one bulk copy that completes its bytes on
+    // rank r's receive barrier.  Each owner waits only on that
+    // barrier, sums the S partials of its groups in split order 0..S-1 from
+    // its own shared memory, applies bias + SiLU and stores.
     const uint32_t recv = sbase + args.recv_offset;
-    if (recv_dedicated) {
-      ptx::cluster_wait();  // all CTAs of the cluster are running
-    } else {
-      ptx::cluster_sync();  // all CTAs have drained the pipeline the buffer reuses
+    const uint32_t stage_out = sbase + args.stage_offset;
+    if (!recv_dedicated) {
+      ptx::cluster_arrive_relaxed();  // this CTA's pipeline is drained
+      ptx::cluster_wait();
     }
     if (!aborted) {
-      for (int q = half; q < chunks; q += 2) {
-        uint32_t r[8];
-        ptx::tmem_ld_32x32b_x8(t_row + static_cast<uint32_t>(q * 8), r);
+      for (int q = q_first; q < chunks; q += q_step) {
+        uint32_t r[16];
+        ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(q * 16), r);
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int g = 2 * q + h;
+        for (int h = 0; h < 4; ++h) {
+          const int g = 4 * q + h;
           if (g < groups) {
             const int owner = group_owner(g, groups, split);
             const int g_lo = (owner * groups) / split;
-            const uint32_t local =
-                recv + ((static_cast<uint32_t>(s) * kTileN + n_local) * pitch4 + (g - g_lo)) * 16u;
-            ptx::st_dsmem_v4(ptx::map_to_rank(local, static_cast<uint32_t>(owner)),
-                             __uint_as_float(r[4 * h]), __uint_as_float(r[4 * h + 1]),
-                             __uint_as_float(r[4 * h + 2]), __uint_as_float(r[4 * h + 3]));
+            const int width = ((owner + 1) * groups) / split - g_lo;
+            // [group][row]: consecutive threads (rows) write consecutive 16 B.
+            uint4* dst = reinterpret_cast<uint4*>(smem + args.stage_offset) + (g * TN + n_local);
+            *dst = make_uint4(r[4 * h], r[4 * h + 1], r[4 * h + 2], r[4 * h + 3]);
           }
         }
         if (args.partial != nullptr && n_ok) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int mm = q * 8 + j;
+          for (int j = 0; j < 16; ++j) {
+            const int mm = q * 16 + j;
             if (mm < mr) {
               args.partial[(static_cast<long long>(s) * args.m + m0 + mm) * args.n + n] =
                   __uint_as_float(r[j]);
@@ -347,22 +392,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    ptx::cluster_sync();  // every push into this CTA is complete and visible
-    if (!aborted) {
-      const int g_lo = (s * groups) / split;
-      const int g_hi = ((s + 1) * groups) / split;
+    ptx::fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0 && !aborted) {
+      for (int owner = 0; owner < split; ++owner) {
+        const int g_lo = (owner * groups) / split;
+        const int width = ((owner + 1) * groups) / split - g_lo;
+        if (width > 0) {
+          const uint32_t bytes = static_cast<uint32_t>(TN * width) * 16u;
+          ptx::bulk_copy_to_peer(ptx::map_to_rank(recv + static_cast<uint32_t>(s) * bytes, static_cast<uint32_t>(owner)),
+                                 stage_out + static_cast<uint32_t>(g_lo * TN) * 16u, bytes,
+                                 ptx::map_to_rank(recv_bar, static_cast<uint32_t>(owner)));
+        }
+      }
+    }
+    const bool received = ptx::mbar_wait_bounded(recv_bar, 0u, aborted ? abort_flag : nullptr, kWaitBudgetNs);
+    if (!received && !aborted) raise(kErrTimeoutEpilogue);
+    if (received && !aborted) {
       const float4* rv = reinterpret_cast<const float4*>(smem + args.recv_offset);
-      for (int j = half; j < g_hi - g_lo; j += 2) {
+      // Thread t reduces W row t % TN (its epilogue row) for owned groups
+      // j = t / TN, t / TN + 256 / TN, ...
+      for (int j = threadIdx.x / TN; j < own_width; j += kThreads / TN) {
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int src = 0; src < split; ++src) {
-          const float4 v = rv[(src * kTileN + n_local) * pitch4 + j];
+          const float4 v = rv[(src * own_width + j) * TN + n_local];
           acc.x += v.x;
           acc.y += v.y;
           acc.z += v.z;
           acc.w += v.w;
         }
         const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-        const int mm0 = 4 * (g_lo + j);
+        const int mm0 = 4 * (own_lo + j);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int mm = mm0 + c;
@@ -372,6 +432,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // Phase 2: a CTA arrives once its own receive barrier has completed, so
+    // passing the wait means every copy of the cluster has landed and no CTA
+    // leaves while a copy from or to it is in flight.  Relaxed: the barrier
+    // orders nothing else (the receive barrier already did).
+    ptx::cluster_arrive_relaxed();
+    ptx::cluster_wait();
   }
 
   // ---- Teardown: after an abort, let this CTA's own TMA loads land first.
@@ -426,34 +492,36 @@ bool encode_kmajor(CUtensorMap* map, CUtensorMapDataType type, const void* base,
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, int BT>
+template <typename T, int BT, int TN>
 cudaError_t set_attrs() {
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kSmemLimit));
 }
 
 template <typename T>
 cudaError_t set_attrs_all() {
   cudaError_t e;
-  if ((e = set_attrs<T, 16>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 32>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 64>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 128>()) != cudaSuccess) return e;
-  return set_attrs<T, 256>();
+  if ((e = set_attrs<T, 16, 256>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 32, 256>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 16, 128>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 32, 128>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 64, 128>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 128, 128>()) != cudaSuccess) return e;
+  return set_attrs<T, 256, 128>();
 }
 
-template <typename T, int BT>
+template <typename T, int BT, int TN>
 cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
   CUtensorMap tmap_w, tmap_a;
   // W = B^T: rows n (pitch b_ns), K contiguous.  A: rows m (pitch a_rs).
   const int64_t w_pitch = p.n > 1 ? p.b_ns * esz : ((p.k * esz + 15) / 16) * 16;
   const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
-  if (!encode_kmajor(&tmap_w, Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, kTileN) ||
+  if (!encode_kmajor(&tmap_w, Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, TN) ||
       !encode_kmajor(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, BT)) {
     return cudaErrorInvalidValue;
   }
-  using Cfg = TcConfig<BT>;
+  using Cfg = TcConfig<BT, TN>;
   TcArgs args;
   args.m = static_cast<int>(p.m);
   args.n = static_cast<int>(p.n);
@@ -468,26 +536,29 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   args.err = err;
   args.flags = p.flags;
   // Shared memory: [pipeline stages][split-K receive buffer][mbarriers].
-  // The receive buffer gets its own region when it fits, otherwise it reuses
-  // the drained stages (one more cluster barrier).
-  uint32_t recv_bytes = 0, pitch4 = 1;
+  // The receive buffer (split x TN rows x owned groups x 16 B) gets its own
+  // region when it fits; otherwise it reuses the drained stages, after one
+  // more cluster barrier.  The send staging buffer (TN rows x all groups x
+  // 16 B) always reuses the drained stages, after the receive buffer.
+  uint32_t recv_bytes = 0, stage_bytes = 0;
   if (split > 1) {
     const uint32_t groups = BT / 4;
     const uint32_t width = (groups + split - 1) / split;
-    pitch4 = (width % 2 == 0) ? width + 1 : width;
-    recv_bytes = static_cast<uint32_t>(split) * kTileN * pitch4 * 16u;
+    recv_bytes = static_cast<uint32_t>(split) * TN * width * 16u;
+    stage_bytes = TN * groups * 16u;
   }
   const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= kSmemLimit;
   args.recv_offset = dedicated ? Cfg::kPipeBytes : 0;
-  args.recv_pitch4 = pitch4;
+  args.stage_offset = dedicated ? 0 : ((recv_bytes + 1023u) & ~1023u);
   args.recv_overlaps = dedicated ? 0 : 1;
-  const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : (Cfg::kPipeBytes > recv_bytes ? Cfg::kPipeBytes : recv_bytes);
+  if (args.stage_offset + stage_bytes > Cfg::kPipeBytes) return cudaErrorInvalidValue;
+  const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : Cfg::kPipeBytes;
   args.barrier_offset = (body + 15u) & ~15u;
   const uint32_t smem_bytes = 1024 + args.barrier_offset + Cfg::kBarrierBytes;
   if (smem_bytes > kSmemLimit) return cudaErrorInvalidValue;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>((p.n + kTileN - 1) / kTileN),
+  cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>((p.n + TN - 1) / TN),
                      static_cast<unsigned>((p.m + BT - 1) / BT));
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
@@ -501,17 +572,24 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT>, tmap_w, tmap_a, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN>, tmap_w, tmap_a, args);
 }
 
 template <typename T>
-cudaError_t launch_bt(const Problem& p, int split, int tile_t, unsigned int* err, cudaStream_t s) {
+cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, unsigned int* err, cudaStream_t s) {
+  if (tile_n == 256) {
+    switch (tile_t) {
+      case 16: return launch_typed<T, 16, 256>(p, split, err, s);
+      case 32: return launch_typed<T, 32, 256>(p, split, err, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (tile_t) {
-    case 16: return launch_typed<T, 16>(p, split, err, s);
-    case 32: return launch_typed<T, 32>(p, split, err, s);
-    case 64: return launch_typed<T, 64>(p, split, err, s);
-    case 128: return launch_typed<T, 128>(p, split, err, s);
-    case 256: return launch_typed<T, 256>(p, split, err, s);
+    case 16: return launch_typed<T, 16, 128>(p, split, err, s);
+    case 32: return launch_typed<T, 32, 128>(p, split, err, s);
+    case 64: return launch_typed<T, 64, 128>(p, split, err, s);
+    case 128: return launch_typed<T, 128, 128>(p, split, err, s);
+    case 256: return launch_typed<T, 256, 128>(p, split, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -524,9 +602,9 @@ cudaError_t tc_prepare_device() {
   return set_attrs_all<__nv_bfloat16>();
 }
 
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, unsigned int* err, cudaStream_t s) {
-  if (p.dtype == GLQ_DTYPE_BF16) return launch_bt<__nv_bfloat16>(p, split, tile_t, err, s);
-  return launch_bt<__half>(p, split, tile_t, err, s);
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, unsigned int* err, cudaStream_t s) {
+  if (p.dtype == GLQ_DTYPE_BF16) return launch_bt<__nv_bfloat16>(p, split, tile_t, tile_n, err, s);
+  return launch_bt<__half>(p, split, tile_t, tile_n, err, s);
 }
 
 }  // namespace glq

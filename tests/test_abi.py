@@ -107,10 +107,14 @@ def test_plan_auto_split_tracks_sm_count():
     assert plan(32, 4096, 4096, sms=148) == ("tc_splitk", 4)
     assert plan(32, 4096, 4096, sms=64) == ("tc_splitk", 2)
     assert plan(32, 4096, 4096, sms=32) == ("tc_tcgen05", 1)
+    assert plan(128, 4096, 4096, sms=148) == ("tc_splitk", 4)
+    # M <= 32 on N >= 8192: 256-row W tiles, 32 tiles -> split 4.
+    assert plan(32, 8192, 8192) == ("tc_splitk", 4)
     # prefill: 16 x 8 = 128 tiles already fill the device.
     assert plan(4096, 1024, 8192) == ("tc_tcgen05", 1)
-    # sharded MLP slice 28672 / 8 = 3584 rows: 28 tiles -> split 5.
-    assert plan(32, 3584, 8192) == ("tc_splitk", 5)
+    # sharded MLP slice 28672 / 8 = 3584 rows: 28 tiles -> split 4 (automatic cap).
+    assert plan(32, 3584, 8192) == ("tc_splitk", 4)
+    assert plan(128, 3584, 8192) == ("tc_splitk", 4)
 
 
 def test_plan_rejects_bad_arguments():
@@ -130,6 +134,7 @@ def test_plan_rejects_bad_arguments():
 
 def test_workspace_bytes():
     assert native.workspace_bytes(32, 4096, 4096, 0) == 4 * 32 * 4096 * 4
+    assert native.workspace_bytes(128, 4096, 4096, 0) == 4 * 128 * 4096 * 4
     assert native.workspace_bytes(8, 4096, 4096, 8) == 8 * 8 * 4096 * 4
     assert native.workspace_bytes(1, 4096, 4096, 0) == 0
     assert native.workspace_bytes(1, 4096, 4096, 4) == 4 * 4096 * 4
@@ -203,4 +208,6 @@ def test_adaptive_path_names_native_kernel():
     from gemm_lab_qualification_b200 import kernels
     assert kernels.adaptive_path(8, 4096, 4096, torch.float16) == "tc_splitk"
     assert kernels.adaptive_path(1, 4096, 4096) == "gemv_m1"
-    assert kernels.adaptive_bias_silu_path(8, 11008, 4096, torch.float16) == "tc_tcgen05"
+    # MLP up-projection: 43 tiles of 256 rows, split 3 -> 129 CTAs.
+    assert kernels.adaptive_bias_silu_path(8, 11008, 4096, torch.float16) == "tc_splitk"
+    assert kernels.adaptive_path(8, 11008, 4096, torch.float16) == "tc_splitk"

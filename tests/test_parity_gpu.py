@@ -333,3 +333,17 @@ def test_pdl_chain_respects_dependencies(cuda_device):
     assert torch.equal(y2.view(torch.int16), ref2.view(torch.int16))
     expected = oracle.linear_reference(host(y1).astype(np.float16), w2, b2, silu=True)
     oracle.compare(host(y2), expected, U_ATOL, U_RTOL)
+
+
+@pytest.mark.parametrize("m", [8, 32])
+def test_wide_layer_256_row_tiles(cuda_device, m):
+    """M <= 32 on N >= 8192 takes 256-row W tiles (two accumulators)."""
+    a, w, bias = workloads.uniform_inputs(m, 8192, 2048)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    out = kernels.triton_bias_silu(da, dw.t(), db)
+    assert kernels.last_path() == ("tc_splitk", 4)
+    oracle.compare(host(out), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+    # ragged N on the same tiles
+    out = kernels.triton_bias_silu(da, dw[:8000].t(), db[:8000])
+    assert kernels.last_path()[0] == "tail"
+    oracle.compare(host(out), oracle.linear_reference(a, w[:8000], bias[:8000], silu=True), U_ATOL, U_RTOL)
