@@ -93,6 +93,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->split = 1;
   c->tile_t = 0;
   c->tile_n = 128;
+  c->stages = 0;
   if (p.m == 0 || p.n == 0) {
     c->path = GLQ_PATH_EMPTY;
     c->kernel = kKernelNone;
@@ -130,7 +131,15 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->tile_n = tc_tile_rows(p.m, p.n);
   const int64_t k_blocks = tc_k_blocks(p.k);
   const int64_t tiles = ((p.n + c->tile_n - 1) / c->tile_n) * ((p.m + c->tile_t - 1) / c->tile_t);
-  int s = split_k > 0 ? split_k : auto_split(tiles, k_blocks, sm_count > 0 ? sm_count : 148);
+  const int sms = sm_count > 0 ? sm_count : 148;
+  int s = split_k > 0 ? split_k : auto_split(tiles, k_blocks, sms);
+  // Two CTAs per SM with an 8-way split when that still fits one wave.
+  if (split_k == 0 && c->tile_n == 128 && c->tile_t <= 32 && tiles * kPairSplit <= 2 * sms &&
+      tiles * kPairSplit > static_cast<int64_t>(s) * tiles && k_blocks >= 2 * kPairSplit) {
+    s = kPairSplit;
+    c->stages = kPairStages;
+  }
+  if (split_k == kPairSplit && c->tile_n == 128 && c->tile_t <= 32) c->stages = kPairStages;
   s = static_cast<int>(std::min<int64_t>(s, k_blocks));
   c->split = std::max(s, 1);
   // Split-K tiles hold at most 128 tokens (the merge buffers must fit in the
@@ -238,7 +247,7 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
     case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
-    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, dev->error_word, s); break;
+    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, dev->error_word, s); break;
     case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
     default: break;
   }
@@ -275,19 +284,20 @@ int glq_splitk_matmul(int dtype, const void* a, const void* b, void* c, int m, i
 
 size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k) {
   if (M <= 0 || N <= 0 || K <= 0 || split_k < 0 || split_k > GLQ_MAX_SPLIT) return 0;
-  int s;
-  if (M == 1) {
-    s = split_k > 0 ? split_k : 1;
-  } else {
-    const int64_t kb = glq::tc_k_blocks(K);
-    const int bt = glq::tc_token_tile(M);
-    const int tn = glq::tc_tile_rows(M, N);
-    const int64_t tiles = ((N + tn - 1) / tn) * ((M + bt - 1) / bt);
-    s = split_k > 0 ? split_k : glq::auto_split(tiles, kb, 148);
-    s = static_cast<int>(std::min<int64_t>(s, kb));
-  }
-  if (s <= 1) return 0;
-  return static_cast<size_t>(s) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
+  // The plan of a K-contiguous problem (A row pitch K, W = B^T row pitch K).
+  Problem p = {};
+  p.dtype = GLQ_DTYPE_F16;
+  p.a_rs = K;
+  p.a_cs = 1;
+  p.b_ks = 1;
+  p.b_ns = K;
+  p.ldy = N;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  Choice c;
+  if (glq::plan_problem(p, split_k, 0, &c) != GLQ_OK || c.split <= 1) return 0;
+  return static_cast<size_t>(c.split) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
 }
 
 const char* glq_path_name(int path) {

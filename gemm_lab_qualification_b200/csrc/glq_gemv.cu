@@ -39,6 +39,7 @@ struct GemvArgs {
   int rows_per_block;
   float* partial;
   unsigned int flags;
+  int a_in_smem;  // 1: the block stages A (K/8 16-byte chunks) in dynamic shared memory
 };
 
 __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilogue) {
@@ -88,10 +89,14 @@ __device__ __forceinline__ void dot8(const uint4& w, const uint4& a, float& acc0
 }
 
 constexpr int kBlockThreadsMax = 256;
+// A is staged in shared memory up to this many bytes (K <= 24576); four
+// blocks per SM still fit.
+constexpr size_t kGemvSmemA = 48 * 1024;
 
 template <typename T, int UNROLL>
 __global__ void __launch_bounds__(kBlockThreadsMax, 4) gemv_kernel(const GemvArgs g) {
   __shared__ float warp_sums[kBlockThreadsMax / 32];
+  extern __shared__ uint4 a_smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int split = g.split;
@@ -122,14 +127,25 @@ __global__ void __launch_bounds__(kBlockThreadsMax, 4) gemv_kernel(const GemvArg
   if (static_w) load_w(c_begin + lane);
   ptx::grid_dependency_wait();
   ptx::grid_launch_dependents();
+  // First weight chunks in flight before anything else, then A staged once
+  // per block in shared memory (every warp reads all of A), then the bias of
+  // this warp's row, so none of these latencies lands at the end.
+  if (!static_w) load_w(c_begin + lane);
+  if (g.a_in_smem) {
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) a_smem[c] = __ldg(av + c);
+  }
+  float bias_v = 0.0f;
+  if (g.epilogue != GLQ_EPILOGUE_NONE && row_ok && part == 0 && lane == 0) {
+    bias_v = Vec<T>::to_f(static_cast<const T*>(g.bias)[n]);
+  }
+  if (g.a_in_smem) __syncthreads();
   if (row_ok) {
-    if (!static_w) load_w(c_begin + lane);
     for (int c = c_begin + lane; c < c_end; c += 32 * UNROLL) {
 #pragma unroll
       for (int u = 0; u < UNROLL; ++u) {
         const int cc = c + u * 32;
         if (cc < c_end) {
-          const uint4 a = __ldg(av + cc);
+          const uint4 a = g.a_in_smem ? a_smem[cc] : __ldg(av + cc);
           dot8<T>(w[u], a, acc0, acc1);
         }
       }
@@ -155,8 +171,6 @@ __global__ void __launch_bounds__(kBlockThreadsMax, 4) gemv_kernel(const GemvArg
       sum += v;
       if (g.partial != nullptr) g.partial[static_cast<long long>(p) * g.n + n] = v;
     }
-    float bias_v = 0.0f;
-    if (g.epilogue != GLQ_EPILOGUE_NONE) bias_v = Vec<T>::to_f(static_cast<const T*>(g.bias)[n]);
     static_cast<T*>(g.y)[n] = Vec<T>::from_f(apply_epilogue(sum, bias_v, g.epilogue));
   }
 }
@@ -180,10 +194,12 @@ cudaError_t launch_gemv(const Problem& p, int split, unsigned int* /*err*/, cuda
   g.rows_per_block = rows;
   g.partial = p.partial;
   g.flags = p.flags;
+  const size_t a_bytes = static_cast<size_t>(p.k / 8) * 16;
+  g.a_in_smem = a_bytes <= kGemvSmemA ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((p.n + rows - 1) / rows), 1, 1);
   cfg.blockDim = dim3(static_cast<unsigned>(rows * warps_per_row * 32), 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = g.a_in_smem ? a_bytes : 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -48,6 +48,7 @@ struct Choice {
   int kernel;   // Kernel below
   int tile_t;   // token tile (MMA N) of the tcgen05 kernel
   int tile_n;   // W rows per CTA of the tcgen05 kernel (128 or 256)
+  int stages;   // TMA ring depth of the tcgen05 kernel (5: two CTAs per SM)
 };
 
 enum Kernel : int {
@@ -74,6 +75,12 @@ inline int tc_tile_rows(int64_t m, int64_t n) { return (m <= 32 && n >= 8192) ? 
 // co-resident on B200); larger clusters may not, which costs a second wave.
 constexpr int kMaxAutoSplit = 4;
 
+// Small token tiles on narrow layers: two CTAs per SM (5-stage ring, under
+// 113 KB of shared memory), so an 8-way split-K cluster still packs one wave
+// (33 clusters of 8 are co-resident at that size).
+constexpr int kPairSplit = 8;
+constexpr int kPairStages = 5;
+
 // Token tile of the tcgen05 kernel for m tokens.
 inline int tc_token_tile(int64_t m) {
   if (m <= 16) return 16;
@@ -89,7 +96,8 @@ cudaError_t launch_gemv(const Problem& p, int split, unsigned int* err, cudaStre
 cudaError_t launch_generic(const Problem& p, cudaStream_t s);
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, unsigned int* err, cudaStream_t s);
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
+                      cudaStream_t s);
 
 // Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).
 cudaError_t tc_prepare_device();

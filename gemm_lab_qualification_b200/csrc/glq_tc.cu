@@ -81,12 +81,15 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilo
 constexpr int kTileK = 64;  // K elements per stage: one 128-byte swizzle row
 constexpr int kThreads = 256;
 constexpr uint32_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
+// Two CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per block.
+constexpr uint32_t kPairSmemBudget = 233472u / 2u - 1024u;
 
 // BT: token tile (MMA N).  TN: W rows per CTA, one M = 128 MMA (and one TMEM
 // accumulator of BT columns) per 128 rows.  A 256-row tile moves W in 32 KB
 // TMA boxes, which streams HBM measurably better than 16 KB boxes at equal
-// bytes in flight; it is used for small token tiles.
-template <int BT, int TN>
+// bytes in flight.  STAGES: depth of the TMA ring; 5 stages of a small token
+// tile keep a CTA under 113 KB of shared memory, so two CTAs share an SM.
+template <int BT, int TN, int STAGES>
 struct TcConfig {
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128 is 16..256 step 16");
   static_assert(TN == 128 || TN == 256, "tile rows are one or two M=128 MMAs");
@@ -94,7 +97,7 @@ struct TcConfig {
   static constexpr uint32_t kWTileBytes = TN * kTileK * 2;
   static constexpr uint32_t kATileBytes = BT * kTileK * 2;
   static constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
-  static constexpr int kStages = TN == 256 ? 4 : (BT <= 64 ? 8 : (BT <= 128 ? 6 : 4));
+  static constexpr int kStages = STAGES;
   static constexpr uint32_t kAccCols = kAcc * BT;
   static constexpr uint32_t kTmemCols =
       kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
@@ -127,11 +130,11 @@ __device__ __forceinline__ int group_owner(int g, int groups, int split) {
   return ((g + 1) * split + groups - 1) / groups - 1;
 }
 
-template <typename T, int BT, int TN>
+template <typename T, int BT, int TN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_a, const TcArgs args) {
-  using Cfg = TcConfig<BT, TN>;
+  using Cfg = TcConfig<BT, TN, STAGES>;
   constexpr uint32_t kWTileBytes = Cfg::kWTileBytes;
   constexpr int kStages = Cfg::kStages;
 
@@ -492,25 +495,27 @@ bool encode_kmajor(CUtensorMap* map, CUtensorMapDataType type, const void* base,
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, int BT, int TN>
+template <typename T, int BT, int TN, int STAGES>
 cudaError_t set_attrs() {
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kSmemLimit));
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
 }
 
 template <typename T>
 cudaError_t set_attrs_all() {
   cudaError_t e;
-  if ((e = set_attrs<T, 16, 256>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 32, 256>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 16, 128>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 32, 128>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 64, 128>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 128, 128>()) != cudaSuccess) return e;
-  return set_attrs<T, 256, 128>();
+  if ((e = set_attrs<T, 16, 256, 4>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 32, 256, 4>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 16, 128, 5>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 32, 128, 5>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 16, 128, 8>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 32, 128, 8>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 64, 128, 8>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 128, 128, 6>()) != cudaSuccess) return e;
+  return set_attrs<T, 256, 128, 4>();
 }
 
-template <typename T, int BT, int TN>
+template <typename T, int BT, int TN, int STAGES>
 cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
   CUtensorMap tmap_w, tmap_a;
@@ -521,7 +526,7 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
       !encode_kmajor(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, BT)) {
     return cudaErrorInvalidValue;
   }
-  using Cfg = TcConfig<BT, TN>;
+  using Cfg = TcConfig<BT, TN, STAGES>;
   TcArgs args;
   args.m = static_cast<int>(p.m);
   args.n = static_cast<int>(p.n);
@@ -547,7 +552,9 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
     recv_bytes = static_cast<uint32_t>(split) * TN * width * 16u;
     stage_bytes = TN * groups * 16u;
   }
-  const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= kSmemLimit;
+  // The 5-stage ring is the two-CTAs-per-SM configuration: keep under half an SM.
+  const uint32_t budget = STAGES == 5 ? kPairSmemBudget : kSmemLimit;
+  const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= budget;
   args.recv_offset = dedicated ? Cfg::kPipeBytes : 0;
   args.stage_offset = dedicated ? 0 : ((recv_bytes + 1023u) & ~1023u);
   args.recv_overlaps = dedicated ? 0 : 1;
@@ -555,7 +562,7 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : Cfg::kPipeBytes;
   args.barrier_offset = (body + 15u) & ~15u;
   const uint32_t smem_bytes = 1024 + args.barrier_offset + Cfg::kBarrierBytes;
-  if (smem_bytes > kSmemLimit) return cudaErrorInvalidValue;
+  if (smem_bytes > budget) return cudaErrorInvalidValue;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>((p.n + TN - 1) / TN),
@@ -572,24 +579,32 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN>, tmap_w, tmap_a, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES>, tmap_w, tmap_a, args);
 }
 
 template <typename T>
-cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, unsigned int* err, cudaStream_t s) {
+cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
+                      cudaStream_t s) {
   if (tile_n == 256) {
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 256>(p, split, err, s);
-      case 32: return launch_typed<T, 32, 256>(p, split, err, s);
+      case 16: return launch_typed<T, 16, 256, 4>(p, split, err, s);
+      case 32: return launch_typed<T, 32, 256, 4>(p, split, err, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (stages == 5) {
+    switch (tile_t) {
+      case 16: return launch_typed<T, 16, 128, 5>(p, split, err, s);
+      case 32: return launch_typed<T, 32, 128, 5>(p, split, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (tile_t) {
-    case 16: return launch_typed<T, 16, 128>(p, split, err, s);
-    case 32: return launch_typed<T, 32, 128>(p, split, err, s);
-    case 64: return launch_typed<T, 64, 128>(p, split, err, s);
-    case 128: return launch_typed<T, 128, 128>(p, split, err, s);
-    case 256: return launch_typed<T, 256, 128>(p, split, err, s);
+    case 16: return launch_typed<T, 16, 128, 8>(p, split, err, s);
+    case 32: return launch_typed<T, 32, 128, 8>(p, split, err, s);
+    case 64: return launch_typed<T, 64, 128, 8>(p, split, err, s);
+    case 128: return launch_typed<T, 128, 128, 6>(p, split, err, s);
+    case 256: return launch_typed<T, 256, 128, 4>(p, split, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -602,9 +617,10 @@ cudaError_t tc_prepare_device() {
   return set_attrs_all<__nv_bfloat16>();
 }
 
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, unsigned int* err, cudaStream_t s) {
-  if (p.dtype == GLQ_DTYPE_BF16) return launch_bt<__nv_bfloat16>(p, split, tile_t, tile_n, err, s);
-  return launch_bt<__half>(p, split, tile_t, tile_n, err, s);
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
+                      cudaStream_t s) {
+  if (p.dtype == GLQ_DTYPE_BF16) return launch_bt<__nv_bfloat16>(p, split, tile_t, tile_n, stages, err, s);
+  return launch_bt<__half>(p, split, tile_t, tile_n, stages, err, s);
 }
 
 }  // namespace glq

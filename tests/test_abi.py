@@ -61,7 +61,7 @@ def plan(m, n, k, a_strides=None, b_strides=None, a_ptr=0, b_ptr=0, split=0, ldy
                        split, sms)
 
 
-@pytest.mark.parametrize("m,expected", [(1, ("gemv_m1", 1)), (8, ("tc_splitk", 4)), (32, ("tc_splitk", 4)),
+@pytest.mark.parametrize("m,expected", [(1, ("gemv_m1", 1)), (8, ("tc_splitk", 8)), (32, ("tc_splitk", 8)),
                                         (128, ("tc_splitk", 4))])
 def test_plan_decode_sweep(m, expected):
     assert plan(m, 4096, 4096) == expected
@@ -104,7 +104,8 @@ def test_plan_split_clamped_to_k_blocks():
 
 
 def test_plan_auto_split_tracks_sm_count():
-    assert plan(32, 4096, 4096, sms=148) == ("tc_splitk", 4)
+    # 32 tiles: two CTAs per SM with an 8-way split (256 CTAs) when 148 SMs.
+    assert plan(32, 4096, 4096, sms=148) == ("tc_splitk", 8)
     assert plan(32, 4096, 4096, sms=64) == ("tc_splitk", 2)
     assert plan(32, 4096, 4096, sms=32) == ("tc_tcgen05", 1)
     assert plan(128, 4096, 4096, sms=148) == ("tc_splitk", 4)
@@ -112,8 +113,8 @@ def test_plan_auto_split_tracks_sm_count():
     assert plan(32, 8192, 8192) == ("tc_splitk", 4)
     # prefill: 16 x 8 = 128 tiles already fill the device.
     assert plan(4096, 1024, 8192) == ("tc_tcgen05", 1)
-    # sharded MLP slice 28672 / 8 = 3584 rows: 28 tiles -> split 4 (automatic cap).
-    assert plan(32, 3584, 8192) == ("tc_splitk", 4)
+    # sharded MLP slice 28672 / 8 = 3584 rows: 28 tiles -> two per SM, split 8.
+    assert plan(32, 3584, 8192) == ("tc_splitk", 8)
     assert plan(128, 3584, 8192) == ("tc_splitk", 4)
 
 
@@ -133,7 +134,7 @@ def test_plan_rejects_bad_arguments():
 
 
 def test_workspace_bytes():
-    assert native.workspace_bytes(32, 4096, 4096, 0) == 4 * 32 * 4096 * 4
+    assert native.workspace_bytes(32, 4096, 4096, 0) == 8 * 32 * 4096 * 4
     assert native.workspace_bytes(128, 4096, 4096, 0) == 4 * 128 * 4096 * 4
     assert native.workspace_bytes(8, 4096, 4096, 8) == 8 * 8 * 4096 * 4
     assert native.workspace_bytes(1, 4096, 4096, 0) == 0
