@@ -161,6 +161,23 @@ class ClockSampler:
                 "power_w_max": max(r["power"] for r in rows), "samples": len(rows), "reasons": sorted(reasons)}
 
 
+def host_threads() -> int:
+    """Cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def use_all_host_threads() -> None:
+    """Let the BLAS behind numpy use every core (torchrun sets OMP_NUM_THREADS=1)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=host_threads(), user_api="blas")
+    except Exception:  # threadpoolctl missing: keep the library default
+        pass
+
+
 def numpy_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -174,6 +191,7 @@ def numpy_threads() -> int:
 def cpu_fragment_timings(m: int, budget_s: float, max_calls: int) -> tuple[list[float], dict]:
     """FP64 SiLU(A @ W^T + b) on the host cores: the oracle's compute core."""
     import numpy as np
+    use_all_host_threads()
     from gemm_lab_qualification_b200 import workloads
     from oracle import reference as oracle
     a, w, bias = workloads.uniform_inputs(m, N_DIM, K_DIM)
@@ -395,30 +413,27 @@ def e2e_public_api(args, torch, dev, rounds: int) -> dict:
 
 def multi_gpu(args, torch, dist, dev, world: int, rank: int) -> dict:
     """Column-parallel fused layer: W split along N, local GEMM, NCCL all-gather."""
-    from gemm_lab_qualification_b200 import kernels, workloads
+    from gemm_lab_qualification_b200 import kernels, sharded, workloads
     from gemm_lab_qualification_b200.evidence import device_measure
     m = args.m
-    if N_DIM % world:
-        raise SystemExit("N must divide by the number of GPUs")
-    ns = N_DIM // world
     a, w, bias = workloads.uniform_inputs(m, N_DIM, K_DIM)
+    layer = sharded.ColumnParallelLinear(w, bias, "silu", device=dev)
+    ns = layer.weight.shape[0]
     props = torch.cuda.get_device_properties(dev)
     l2 = int(getattr(props, "L2_cache_size", 126 * 2 ** 20))
     shard_bytes = ns * K_DIM * 2
     copies = args.copies or max(4, math.ceil(3 * l2 / shard_bytes))
     da = a.to(dev)
-    ws = [w[rank * ns:(rank + 1) * ns].to(dev) for _ in range(copies)]
-    db = bias[rank * ns:(rank + 1) * ns].to(dev)
+    ws = [layer.weight.clone() for _ in range(copies)]
     local = torch.empty((m, ns), dtype=torch.float16, device=dev)
     gathered = torch.empty((world, m, ns), dtype=torch.float16, device=dev)
     y = torch.empty((m, N_DIM), dtype=torch.float16, device=dev)
     it = {"i": 0}
 
     def step():
-        kernels.triton_bias_silu_into(da, ws[it["i"] % copies].t(), db, local)
+        kernels.triton_bias_silu_into(da, ws[it["i"] % copies].t(), layer.bias, local)
         it["i"] += 1
-        dist.all_gather_into_tensor(gathered, local)
-        y.view(m, world, ns).copy_(gathered.permute(1, 0, 2))
+        sharded.gather_columns(local, y, gathered=gathered)
 
     step()
     torch.cuda.synchronize()

@@ -347,3 +347,19 @@ def test_wide_layer_256_row_tiles(cuda_device, m):
     out = kernels.triton_bias_silu(da, dw[:8000].t(), db[:8000])
     assert kernels.last_path()[0] == "tail"
     oracle.compare(host(out), oracle.linear_reference(a, w[:8000], bias[:8000], silu=True), U_ATOL, U_RTOL)
+
+
+def test_column_parallel_single_rank(cuda_device, tmp_path):
+    """The sharded layer on a one-rank NCCL group equals the unsharded call."""
+    import torch.distributed as dist
+    from gemm_lab_qualification_b200 import sharded
+    store = dist.FileStore(str(tmp_path / "store"), 1)
+    dist.init_process_group("nccl", store=store, rank=0, world_size=1, device_id=cuda_device)
+    try:
+        a, w, bias = workloads.uniform_inputs(32, 4096, 4096)
+        layer = sharded.ColumnParallelLinear(w, bias, "silu", device=cuda_device)
+        y = layer(a.to(cuda_device))
+        torch.cuda.synchronize()
+        oracle.compare(host(y), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+    finally:
+        dist.destroy_process_group()
