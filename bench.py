@@ -255,7 +255,9 @@ def single_gpu(args, torch, dev) -> dict:
         a, w, bias = workloads.uniform_inputs(m, N_DIM, K_DIM)
         da, db = a.to(dev), bias.to(dev)
         ws = [w.to(dev) for _ in range(copies)]
-        state[m] = {"a": da, "w": ws, "bias": db, "fused": torch.empty((m, N_DIM), dtype=torch.float16, device=dev),
+        # The lab harness's own operand layout, B = [K, N] row-major.
+        ws_kn = [w.t().contiguous().to(dev) for _ in range(copies)]
+        state[m] = {"a": da, "w": ws, "w_kn": ws_kn, "bias": db, "fused": torch.empty((m, N_DIM), dtype=torch.float16, device=dev),
                     "plain": torch.empty((m, N_DIM), dtype=torch.float16, device=dev), "i": 0}
 
     # Gate before timing (the harness refuses to time wrong output): torch
@@ -273,6 +275,12 @@ def single_gpu(args, torch, dev) -> dict:
         err = (st["plain"].float() - ref).abs()
         if not bool((err <= 0.02 + 0.002 * ref.abs()).all()):
             raise SystemExit(f"correctness gate failed (plain) at M={m}")
+        kernels.triton_bias_silu_into(st["a"], st["w_kn"][0], st["bias"], st["fused"])
+        paths[f"kn{m}"] = kernels.last_path()
+        ref = torch.nn.functional.silu(st["a"].float() @ st["w_kn"][0].float() + st["bias"].float())
+        err = (st["fused"].float() - ref).abs()
+        if not bool((err <= 0.02 + 0.002 * ref.abs()).all()):
+            raise SystemExit(f"correctness gate failed (B = [K, N]) at M={m}")
     torch.cuda.synchronize()
 
     def call(m, variant, rotate=True):
@@ -314,6 +322,19 @@ def single_gpu(args, torch, dev) -> dict:
 
     cublas = device_measure({f"{v}/m{m}": vendor(m, v) for m in sweep_m for v in ("fused", "plain")},
                             rounds=max(10, args.steps // 3), inner=args.inner)
+
+    # The fused call on the lab's own B = [K, N] operand (MN-major W tiles).
+    def b_kn(m):
+        st = state[m]
+
+        def run():
+            w_kn = st["w_kn"][st["i"] % copies]
+            st["i"] += 1
+            kernels.triton_bias_silu_into(st["a"], w_kn, st["bias"], st["fused"])
+        return run
+
+    kn = device_measure({f"fused/m{m}": b_kn(m) for m in sweep_m}, rounds=max(10, args.steps // 3),
+                        inner=args.inner)
     # Launch modes of the fused calls: without programmatic dependent launch,
     # and with the inference declaration that W is static.
     modes = {}
@@ -350,6 +371,8 @@ def single_gpu(args, torch, dev) -> dict:
             row[f"fused_{label}_p50_us"] = statistics.median(samples[f"fused/m{m}"]) * 1e3
         for v in ("fused", "plain"):
             row[f"cublas_{v}_p50_us"] = statistics.median(cublas[f"{v}/m{m}"]) * 1e3
+        row["fused_b_kn_p50_us"] = statistics.median(kn[f"fused/m{m}"]) * 1e3
+        row["b_kn_path"] = paths[f"kn{m}"][0]
         sweep[str(m)] = row
 
     head = sweep[str(args.m)]

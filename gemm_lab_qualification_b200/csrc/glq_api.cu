@@ -94,6 +94,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->tile_t = 0;
   c->tile_n = 128;
   c->stages = 0;
+  c->w_mn = 0;
   if (p.m == 0 || p.n == 0) {
     c->path = GLQ_PATH_EMPTY;
     c->kernel = kKernelNone;
@@ -105,22 +106,30 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
     return GLQ_OK;
   }
   constexpr int64_t esz = 2;
-  const bool unit_inner = (p.a_cs == 1 || p.k == 1) && (p.b_ks == 1 || p.k == 1);
-  if (!unit_inner) {
+  // W = B^T is K-contiguous (a linear layer's weight) or N-contiguous (the
+  // lab's B = [K, N] row-major); anything else goes to the generic kernel.
+  const bool a_unit = p.a_cs == 1 || p.k == 1;
+  const bool w_kmajor = p.b_ks == 1 || p.k == 1;
+  const bool w_mnmajor = !w_kmajor && (p.b_ns == 1 || p.n == 1);
+  if (!a_unit || (!w_kmajor && !w_mnmajor)) {
     c->path = GLQ_PATH_STRIDED;
     c->kernel = kKernelGeneric;
     return GLQ_OK;
   }
   // TMA / 128-bit loads: 16-byte aligned bases and row pitches, rows that do
   // not overlap.
-  const bool w_ok = aligned16(p.b) && (p.n == 1 || (p.b_ns > 0 && (p.b_ns * esz) % 16 == 0 && p.b_ns >= p.k));
+  const bool w_ok =
+      aligned16(p.b) &&
+      (w_kmajor ? (p.n == 1 || (p.b_ns > 0 && (p.b_ns * esz) % 16 == 0 && p.b_ns >= p.k))
+                : (p.b_ks > 0 && (p.b_ks * esz) % 16 == 0 && p.b_ks >= p.n));
   const bool a_ok = aligned16(p.a) && (p.m == 1 || (p.a_rs > 0 && (p.a_rs * esz) % 16 == 0 && p.a_rs >= p.k));
   if (!w_ok || !a_ok) {
     c->path = GLQ_PATH_UNALIGNED;
     c->kernel = kKernelGeneric;
     return GLQ_OK;
   }
-  if (p.m == 1) {
+  c->w_mn = w_mnmajor ? 1 : 0;
+  if (p.m == 1 && w_kmajor) {
     c->kernel = kKernelGemv;
     c->split = split_k > 0 ? split_k : 1;
     c->path = (p.k % 8 != 0) ? GLQ_PATH_TAIL : GLQ_PATH_GEMV_M1;
@@ -147,6 +156,8 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   if (c->split > 1 && c->tile_t > 128) c->tile_t = 128;
   if (p.n % 128 != 0 || p.k % 64 != 0) {
     c->path = GLQ_PATH_TAIL;
+  } else if (c->w_mn) {
+    c->path = GLQ_PATH_TC_KN;
   } else {
     c->path = c->split > 1 ? GLQ_PATH_TC_SPLITK : GLQ_PATH_TC;
   }
@@ -247,7 +258,8 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
     case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
-    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, dev->error_word, s); break;
+    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, dev->error_word, s);
+      break;
     case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
     default: break;
   }
@@ -284,7 +296,8 @@ int glq_splitk_matmul(int dtype, const void* a, const void* b, void* c, int m, i
 
 size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k) {
   if (M <= 0 || N <= 0 || K <= 0 || split_k < 0 || split_k > GLQ_MAX_SPLIT) return 0;
-  // The plan of a K-contiguous problem (A row pitch K, W = B^T row pitch K).
+  // The larger of the plans of a K-contiguous W (row pitch K) and an
+  // N-contiguous B = [K, N] (row pitch N); they differ only at M == 1.
   Problem p = {};
   p.dtype = GLQ_DTYPE_F16;
   p.a_rs = K;
@@ -295,9 +308,17 @@ size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k) {
   p.m = M;
   p.n = N;
   p.k = K;
-  Choice c;
-  if (glq::plan_problem(p, split_k, 0, &c) != GLQ_OK || c.split <= 1) return 0;
-  return static_cast<size_t>(c.split) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
+  int split = 1;
+  for (int layout = 0; layout < 2; ++layout) {
+    if (layout == 1) {
+      p.b_ks = N;
+      p.b_ns = 1;
+    }
+    Choice c;
+    if (glq::plan_problem(p, split_k, 0, &c) == GLQ_OK) split = std::max(split, c.split);
+  }
+  if (split <= 1) return 0;
+  return static_cast<size_t>(split) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
 }
 
 const char* glq_path_name(int path) {
@@ -310,6 +331,7 @@ const char* glq_path_name(int path) {
     case GLQ_PATH_TAIL: return "tail";
     case GLQ_PATH_STRIDED: return "strided";
     case GLQ_PATH_UNALIGNED: return "unaligned";
+    case GLQ_PATH_TC_KN: return "tc_kn";
     default: return "unknown";
   }
 }

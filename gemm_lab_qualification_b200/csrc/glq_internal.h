@@ -49,6 +49,7 @@ struct Choice {
   int tile_t;   // token tile (MMA N) of the tcgen05 kernel
   int tile_n;   // W rows per CTA of the tcgen05 kernel (128 or 256)
   int stages;   // TMA ring depth of the tcgen05 kernel (5: two CTAs per SM)
+  int w_mn;     // 1: W = B^T is N-contiguous (B = [K, N]); MN-major W tiles
 };
 
 enum Kernel : int {
@@ -96,8 +97,8 @@ cudaError_t launch_gemv(const Problem& p, int split, unsigned int* err, cudaStre
 cudaError_t launch_generic(const Problem& p, cudaStream_t s);
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
-                      cudaStream_t s);
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
+                      unsigned int* err, cudaStream_t s);
 
 // Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).
 cudaError_t tc_prepare_device();

@@ -186,14 +186,29 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_byte_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 with FP32 accumulation, both operands
-// K-major.  ab_format: 0 = FP16, 1 = BF16.  Bit layout: [4,6) D format
-// (1 = F32), [7,10) A format, [10,13) B format, bit 15/16 A/B major
-// (0 = K), [17,23) N >> 3, [24,29) M >> 4.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int mma_m, int mma_n, int ab_format) {
+// Shared-memory descriptor for an MN-major operand tile written by TMA with
+// 128-byte swizzle as boxes of 64 MN elements x 64 K rows: a K row of one
+// box is 128 contiguous bytes, 8-row K groups are 1024 B apart (stride byte
+// offset) and the second 64-element MN half is the next box, 8192 B later
+// (leading byte offset).  Same version / layout-type fields as above.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_byte_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(8192u >> 4) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with FP32 accumulation.  ab_format:
+// 0 = FP16, 1 = BF16.  a_mn_major: 1 when the A operand is MN-major.  Bit
+// layout: [4,6) D format (1 = F32), [7,10) A format, [10,13) B format, bit
+// 15/16 A/B major (0 = K, 1 = MN), [17,23) N >> 3, [24,29) M >> 4.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int mma_m, int mma_n, int ab_format, int a_mn_major = 0) {
   return (1u << 4) | (static_cast<uint32_t>(ab_format) << 7) |
-         (static_cast<uint32_t>(ab_format) << 10) | (static_cast<uint32_t>(mma_n >> 3) << 17) |
-         (static_cast<uint32_t>(mma_m >> 4) << 24);
+         (static_cast<uint32_t>(ab_format) << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
+         (static_cast<uint32_t>(mma_n >> 3) << 17) | (static_cast<uint32_t>(mma_m >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- cluster

@@ -28,6 +28,11 @@
 //     barrier set-up and TMEM allocation with the predecessor's tail.  With
 //     GLQ_FLAG_STATIC_WEIGHTS the first W stages are requested before the
 //     wait.
+//   * W layouts: K-contiguous W [N, K] (a linear layer's weight) is loaded as
+//     one 64(k) x TN box per stage and described K-major; the lab's own
+//     B = [K, N] row-major (N contiguous) is loaded as TN/64 boxes of
+//     64(n) x 64(k) and described MN-major to the MMA (WMN = true).  Both
+//     land 128-byte swizzled; only the descriptors and the box shape differ.
 //   * Every mbarrier wait is bounded (glq_ptx.cuh); on expiry the CTA raises
 //     a bit in the device error word, stops issuing work, drains its own
 //     in-flight TMA loads (bounded), still takes part in both cluster
@@ -79,6 +84,7 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilo
 }
 
 constexpr int kTileK = 64;  // K elements per stage: one 128-byte swizzle row
+constexpr uint32_t kMnBoxBytes = 64u * kTileK * 2u;  // one 64(n) x 64(k) MN-major W box
 constexpr int kThreads = 256;
 constexpr uint32_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
 // Two CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per block.
@@ -130,7 +136,7 @@ __device__ __forceinline__ int group_owner(int g, int groups, int split) {
   return ((g + 1) * split + groups - 1) / groups - 1;
 }
 
-template <typename T, int BT, int TN, int STAGES>
+template <typename T, int BT, int TN, int STAGES, bool WMN>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_a, const TcArgs args) {
@@ -185,7 +191,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int stage = i % kStages;
     const uint32_t w_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
     ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
-    ptx::tma_load_2d(w_dst, &tmap_w, (kb_begin + i) * kTileK, tile_n * TN, full_bar(stage), pol_w);
+    if constexpr (WMN) {
+      // TN/64 boxes of 64 N-contiguous W rows x 64 K rows, 8 KB apart.
+#pragma unroll
+      for (int j = 0; j < TN / 64; ++j) {
+        ptx::tma_load_2d(w_dst + static_cast<uint32_t>(j) * kMnBoxBytes, &tmap_w, tile_n * TN + 64 * j,
+                         (kb_begin + i) * kTileK, full_bar(stage), pol_w);
+      }
+    } else {
+      ptx::tma_load_2d(w_dst, &tmap_w, (kb_begin + i) * kTileK, tile_n * TN, full_bar(stage), pol_w);
+    }
   };
   auto issue_a = [&](int i) {
     const int stage = i % kStages;
@@ -290,7 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---- MMA issuer: per 128 W rows h, D_h[128 x BT] += W_h[128 x 64] * A[BT x 64]^T;
       // accumulator h occupies TMEM columns [h*BT, (h+1)*BT).
-      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT, Elem<T>::kFormat);
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT, Elem<T>::kFormat, WMN ? 1 : 0);
+      // Descriptor start-address step (16-byte units) per K = 16 MMA: 32 B
+      // along a K-major swizzled row, or 16 K rows of 128 B when MN-major.
+      constexpr uint32_t kWStep = WMN ? 128u : 2u;
       for (int i = 0; i < nkb; ++i) {
         const int stage = i % kStages;
         const uint32_t round = static_cast<uint32_t>(i / kStages);
@@ -300,16 +318,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after_sync();
         const uint32_t w_src = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
-        const uint64_t w_desc = ptx::umma_desc_k_sw128(w_src);
+        const uint64_t w_desc = WMN ? ptx::umma_desc_mn_sw128(w_src) : ptx::umma_desc_k_sw128(w_src);
         const uint64_t a_desc = ptx::umma_desc_k_sw128(w_src + kWTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kTileK / 16; ++kk) {
-          // Each MMA consumes K = 16 (32 bytes); the descriptor start address
-          // is in 16-byte units, so step by 2 inside the swizzled row.  The
-          // 128-row halves of a 256-row W tile are 16 KB (1024 units) apart.
+          // Each MMA consumes K = 16.  The 128-row halves of a 256-row W
+          // tile are 16 KB (1024 units) apart in both layouts.
 #pragma unroll
           for (int h = 0; h < Cfg::kAcc; ++h) {
-            ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT), w_desc + 1024u * h + 2u * kk,
+            ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT), w_desc + 1024u * h + kWStep * kk,
                             a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
           }
         }
@@ -480,14 +497,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return g_encode;
 }
 
-// 2-D K-major map: rows x cols(K) with a row pitch in bytes, box rows x 64.
-bool encode_kmajor(CUtensorMap* map, CUtensorMapDataType type, const void* base, int64_t cols,
-                   int64_t rows, int64_t row_pitch_bytes, uint32_t box_rows) {
+// 2-D map of a row-major matrix rows x cols (cols contiguous) with a row
+// pitch in bytes; box box_rows x box_cols, 128-byte swizzle, OOB zero fill.
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int64_t cols, int64_t rows,
+               int64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = encoder();
   if (encode == nullptr) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_pitch_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), box_rows};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -497,7 +515,10 @@ bool encode_kmajor(CUtensorMap* map, CUtensorMapDataType type, const void* base,
 
 template <typename T, int BT, int TN, int STAGES>
 cudaError_t set_attrs() {
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES>,
+  cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, true>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
 }
 
@@ -515,15 +536,22 @@ cudaError_t set_attrs_all() {
   return set_attrs<T, 256, 128, 4>();
 }
 
-template <typename T, int BT, int TN, int STAGES>
+template <typename T, int BT, int TN, int STAGES, bool WMN>
 cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
   CUtensorMap tmap_w, tmap_a;
-  // W = B^T: rows n (pitch b_ns), K contiguous.  A: rows m (pitch a_rs).
-  const int64_t w_pitch = p.n > 1 ? p.b_ns * esz : ((p.k * esz + 15) / 16) * 16;
   const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
-  if (!encode_kmajor(&tmap_w, Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, TN) ||
-      !encode_kmajor(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, BT)) {
+  bool ok;
+  if constexpr (WMN) {
+    // B = [K, N]: rows k (pitch b_ks), N contiguous; boxes 64(n) x 64(k).
+    ok = encode_2d(&tmap_w, Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
+  } else {
+    // W = B^T: rows n (pitch b_ns), K contiguous; boxes 64(k) x TN.
+    const int64_t w_pitch = p.n > 1 ? p.b_ns * esz : ((p.k * esz + 15) / 16) * 16;
+    ok = encode_2d(&tmap_w, Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, kTileK, TN);
+  }
+  // A: rows m (pitch a_rs), K contiguous; boxes 64(k) x BT.
+  if (!ok || !encode_2d(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, kTileK, BT)) {
     return cudaErrorInvalidValue;
   }
   using Cfg = TcConfig<BT, TN, STAGES>;
@@ -579,32 +607,32 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES>, tmap_w, tmap_a, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN>, tmap_w, tmap_a, args);
 }
 
-template <typename T>
+template <typename T, bool WMN>
 cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
                       cudaStream_t s) {
   if (tile_n == 256) {
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 256, 4>(p, split, err, s);
-      case 32: return launch_typed<T, 32, 256, 4>(p, split, err, s);
+      case 16: return launch_typed<T, 16, 256, 4, WMN>(p, split, err, s);
+      case 32: return launch_typed<T, 32, 256, 4, WMN>(p, split, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
   if (stages == 5) {
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 128, 5>(p, split, err, s);
-      case 32: return launch_typed<T, 32, 128, 5>(p, split, err, s);
+      case 16: return launch_typed<T, 16, 128, 5, WMN>(p, split, err, s);
+      case 32: return launch_typed<T, 32, 128, 5, WMN>(p, split, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (tile_t) {
-    case 16: return launch_typed<T, 16, 128, 8>(p, split, err, s);
-    case 32: return launch_typed<T, 32, 128, 8>(p, split, err, s);
-    case 64: return launch_typed<T, 64, 128, 8>(p, split, err, s);
-    case 128: return launch_typed<T, 128, 128, 6>(p, split, err, s);
-    case 256: return launch_typed<T, 256, 128, 4>(p, split, err, s);
+    case 16: return launch_typed<T, 16, 128, 8, WMN>(p, split, err, s);
+    case 32: return launch_typed<T, 32, 128, 8, WMN>(p, split, err, s);
+    case 64: return launch_typed<T, 64, 128, 8, WMN>(p, split, err, s);
+    case 128: return launch_typed<T, 128, 128, 6, WMN>(p, split, err, s);
+    case 256: return launch_typed<T, 256, 128, 4, WMN>(p, split, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -617,10 +645,14 @@ cudaError_t tc_prepare_device() {
   return set_attrs_all<__nv_bfloat16>();
 }
 
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
-                      cudaStream_t s) {
-  if (p.dtype == GLQ_DTYPE_BF16) return launch_bt<__nv_bfloat16>(p, split, tile_t, tile_n, stages, err, s);
-  return launch_bt<__half>(p, split, tile_t, tile_n, stages, err, s);
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
+                      unsigned int* err, cudaStream_t s) {
+  if (p.dtype == GLQ_DTYPE_BF16) {
+    return w_mn ? launch_bt<__nv_bfloat16, true>(p, split, tile_t, tile_n, stages, err, s)
+                : launch_bt<__nv_bfloat16, false>(p, split, tile_t, tile_n, stages, err, s);
+  }
+  return w_mn ? launch_bt<__half, true>(p, split, tile_t, tile_n, stages, err, s)
+              : launch_bt<__half, false>(p, split, tile_t, tile_n, stages, err, s);
 }
 
 }  // namespace glq

@@ -70,7 +70,9 @@ enum glq_path {
   GLQ_PATH_TAIL = 5,      /* tcgen05 or GEMV kernel on a ragged N/K edge */
   GLQ_PATH_STRIDED = 6,   /* generic kernel: non-unit inner stride */
   GLQ_PATH_UNALIGNED = 7, /* generic kernel: rows or base not 16-B aligned */
-  GLQ_PATH_COUNT = 8
+  GLQ_PATH_TC_KN = 8,     /* tcgen05 GEMM with an N-contiguous B = [K, N]
+                             (the lab's own layout): MN-major W tiles */
+  GLQ_PATH_COUNT = 9
 };
 
 enum glq_status {

@@ -79,10 +79,19 @@ def test_plan_boundaries():
     # padded rows (K + 8) keep 16-byte pitches.
     assert plan(32, 4096, 4096, a_strides=(4104, 1))[0] == "tc_splitk"
     assert plan(32, 4096, 4096, b_strides=(1, 4104))[0] == "tc_splitk"
-    # transposed A, the reference's own B = [K, N] layout -> generic kernel.
+    # transposed A -> generic kernel.
     assert plan(32, 4096, 4096, a_strides=(1, 32))[0] == "strided"
-    assert plan(32, 4096, 4096, b_strides=(4096, 1))[0] == "strided"
-    assert plan(1, 4096, 4096, b_strides=(4096, 1))[0] == "strided"
+    # the reference's own B = [K, N] row-major layout -> MN-major tensor-core path.
+    assert plan(32, 4096, 4096, b_strides=(4096, 1)) == ("tc_kn", 8)
+    assert plan(1, 4096, 4096, b_strides=(4096, 1)) == ("tc_kn", 8)
+    assert plan(128, 4096, 4096, b_strides=(4096, 1)) == ("tc_kn", 4)
+    # B = [K, N] with a ragged N in 16-byte-pitched rows: tails on the same kernel.
+    assert plan(17, 257, 131, a_strides=(136, 1), b_strides=(264, 1)) == ("tail", 1)
+    assert plan(32, 4093, 4096, b_strides=(4096, 1)) == ("tail", 8)
+    # B = [K, N] rows not 16-byte pitched (N = 4093 contiguous) -> generic kernel.
+    assert plan(32, 4093, 4096, b_strides=(4093, 1))[0] == "unaligned"
+    # neither operand dimension contiguous -> generic kernel.
+    assert plan(32, 4096, 4096, b_strides=(2, 8192))[0] == "strided"
     # base one element off 16-byte alignment.
     assert plan(32, 4096, 4096, a_ptr=2)[0] == "unaligned"
     assert plan(1, 4096, 4096, b_ptr=2)[0] == "unaligned"
@@ -137,7 +146,9 @@ def test_workspace_bytes():
     assert native.workspace_bytes(32, 4096, 4096, 0) == 8 * 32 * 4096 * 4
     assert native.workspace_bytes(128, 4096, 4096, 0) == 4 * 128 * 4096 * 4
     assert native.workspace_bytes(8, 4096, 4096, 8) == 8 * 8 * 4096 * 4
-    assert native.workspace_bytes(1, 4096, 4096, 0) == 0
+    # M = 1: the K-contiguous GEMV does not split, B = [K, N] takes the
+    # tensor-core path with an 8-way split; the size covers both layouts.
+    assert native.workspace_bytes(1, 4096, 4096, 0) == 8 * 1 * 4096 * 4
     assert native.workspace_bytes(1, 4096, 4096, 4) == 4 * 4096 * 4
     assert native.workspace_bytes(32, 4096, 4096, 1) == 0
     assert native.workspace_bytes(0, 4096, 4096, 4) == 0

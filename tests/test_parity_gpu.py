@@ -252,13 +252,82 @@ def test_splitk_plan_and_default(cuda_device):
 
 # ------------------------------------------------------------------ layouts, dtypes, ops
 
-def test_reference_layout_b_kn(cuda_device):
-    """The lab's own B = [K, N] row-major operand is an explicit GPU path."""
-    a, w, bias = workloads.uniform_inputs(8, 4096, 4096)
-    da, db_kn, dbias = a.to(cuda_device), w.t().contiguous().to(cuda_device), bias.to(cuda_device)
-    out = kernels.triton_bias_silu(da, db_kn, dbias)
-    assert kernels.last_path()[0] == "strided"
+@pytest.mark.parametrize("m", [1, 8, 32, 128])
+def test_reference_layout_b_kn(cuda_device, m):
+    """The lab's own B = [K, N] row-major operand (qualification.py:63-64,
+    kernels.py:148-171): MN-major W tiles on the tcgen05 path, same gate."""
+    a, w, bias = workloads.uniform_inputs(m, 4096, 4096)
+    da, dw, dbias = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    db_kn = dw.t().contiguous()
+    fused = kernels.triton_bias_silu(da, db_kn, dbias)
+    assert kernels.last_path()[0] == "tc_kn"
+    oracle.compare(host(fused), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+    guard, out = guarded_output(m, 4096, torch.float16, cuda_device)
+    kernels.triton_matmul_into(da, db_kn, out)
+    assert kernels.last_path()[0] == "tc_kn"
+    oracle.compare(host(out), oracle.linear_reference(a, w), U_ATOL, U_RTOL)
+    assert_guard_intact(guard, m, 4096)
+    if m > 1:
+        # Same tiles, split and MMA sequence as the K-contiguous operand.
+        fused_k = kernels.triton_bias_silu(da, dw.t(), dbias)
+        assert kernels.last_path()[1] == kernels.planned_path(da, db_kn)[1]
+        assert torch.equal(fused.view(torch.int16), fused_k.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 257, 131), (129, 257, 65), (17, 31, 13), (300, 200, 520),
+                                   (2, 128, 64), (1, 4093, 4096), (512, 512, 512)])
+def test_b_kn_tails_in_padded_rows(cuda_device, m, n, k):
+    """B = [K, N] with ragged M/N/K in 16-byte-pitched rows (OOB zero fill)."""
+    g = torch.Generator().manual_seed(m * 7919 + n * 31 + k)
+    a = (torch.rand((m, k), generator=g) - .5).half()
+    w = (torch.rand((n, k), generator=g) - .5).half()
+    bias = (torch.rand((n,), generator=g) - .5).half()
+    da = padded_pitch_view(a, cuda_device)
+    db_kn = padded_pitch_view(w.t().contiguous(), cuda_device)
+    pitch = ((n + 7) // 8) * 8 + 8
+    guard, out = guarded_output(m, n, torch.float16, cuda_device, pitch=pitch)
+    kernels.triton_bias_silu_into(da, db_kn, bias.to(cuda_device), out)
+    ragged = n % 128 != 0 or k % 64 != 0
+    assert kernels.last_path()[0] == ("tail" if ragged else "tc_kn")
     oracle.compare(host(out), oracle.linear_reference(a, w, bias, silu=True), U_ATOL, U_RTOL)
+    assert_guard_intact(guard, m, n, pitch=pitch)
+
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("split", [2, 4, 8])
+def test_b_kn_split_probe(cuda_device, m, split):
+    """Split-K on B = [K, N]: partial write-back and the fixed-order merge."""
+    a, w, _ = workloads.uniform_inputs(m, 4096, 4096)
+    da, db_kn = a.to(cuda_device), w.t().contiguous().to(cuda_device)
+    partial = torch.full((split, m, 4096), float("nan"), dtype=torch.float32, device=cuda_device)
+    out = torch.empty((m, 4096), dtype=torch.float16, device=cuda_device)
+    kernels.triton_splitk_matmul_into(da, db_kn, partial, out, split)
+    assert kernels.last_path() == ("tc_kn", split)
+    oracle.compare(host(out), oracle.linear_reference(a, w), U_ATOL, U_RTOL)
+    merged = partial[0].clone()
+    for s in range(1, split):
+        merged = merged + partial[s]
+    assert torch.equal(merged.half().view(torch.int16), out.view(torch.int16))
+
+
+def test_native_launch_surface_b_kn(cuda_device):
+    """glq_matmul / glq_splitk_matmul: the lab's launch_X(a, b, c, m, n, k, stream)
+    with B = [K, N] row-major (csrc/ptx_mma.cuh:220-965)."""
+    lib = native.library()
+    m, n, k = 32, 4096, 4096
+    a, w, _ = workloads.uniform_inputs(m, n, k)
+    da, db_kn = a.to(cuda_device), w.t().contiguous().to(cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    c = torch.empty((m, n), dtype=torch.float16, device=cuda_device)
+    assert lib.glq_matmul(0, da.data_ptr(), db_kn.data_ptr(), c.data_ptr(), m, n, k, stream) == 0
+    c2 = torch.empty_like(c)
+    partial = torch.empty((4, m, n), dtype=torch.float32, device=cuda_device)
+    assert lib.glq_splitk_matmul(0, da.data_ptr(), db_kn.data_ptr(), c2.data_ptr(), m, n, k,
+                                 partial.data_ptr(), 4, stream) == 0
+    torch.cuda.synchronize()
+    expected = oracle.linear_reference(a, w)
+    oracle.compare(host(c), expected, U_ATOL, U_RTOL)
+    oracle.compare(host(c2), expected, U_ATOL, U_RTOL)
 
 
 @pytest.mark.parametrize("m", [1, 32])
