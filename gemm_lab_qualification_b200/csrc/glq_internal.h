@@ -76,11 +76,12 @@ inline int tc_tile_rows(int64_t m, int64_t n) { return (m <= 32 && n >= 8192) ? 
 // co-resident on B200); larger clusters may not, which costs a second wave.
 constexpr int kMaxAutoSplit = 4;
 
-// Small token tiles on narrow layers: two CTAs per SM (5-stage ring, under
-// 113 KB of shared memory), so an 8-way split-K cluster still packs one wave
-// (33 clusters of 8 are co-resident at that size).
+// Small token tiles on narrow layers: two CTAs per SM (4-stage ring plus a
+// dedicated split-K receive buffer, under 113 KB of shared memory), so an
+// 8-way split-K cluster still packs one wave (33 clusters of 8 are
+// co-resident at that size).
 constexpr int kPairSplit = 8;
-constexpr int kPairStages = 5;
+constexpr int kPairStages = 4;
 
 // Token tile of the tcgen05 kernel for m tokens.
 inline int tc_token_tile(int64_t m) {

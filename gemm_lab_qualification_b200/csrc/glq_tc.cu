@@ -93,8 +93,9 @@ constexpr uint32_t kPairSmemBudget = 233472u / 2u - 1024u;
 // BT: token tile (MMA N).  TN: W rows per CTA, one M = 128 MMA (and one TMEM
 // accumulator of BT columns) per 128 rows.  A 256-row tile moves W in 32 KB
 // TMA boxes, which streams HBM measurably better than 16 KB boxes at equal
-// bytes in flight.  STAGES: depth of the TMA ring; 5 stages of a small token
-// tile keep a CTA under 113 KB of shared memory, so two CTAs share an SM.
+// bytes in flight.  STAGES: depth of the TMA ring; 4 stages of a small token
+// tile plus the split-K receive buffer keep a CTA under 113 KB of shared
+// memory, so two CTAs share an SM.
 template <int BT, int TN, int STAGES>
 struct TcConfig {
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128 is 16..256 step 16");
@@ -129,12 +130,6 @@ struct TcArgs {
   uint32_t barrier_offset;  // mbarriers, bytes from the aligned base
   unsigned int flags;       // glq_flags
 };
-
-// Owner rank of 4-column group g when G groups are dealt to S ranks as
-// [r*G/S, (r+1)*G/S).
-__device__ __forceinline__ int group_owner(int g, int groups, int split) {
-  return ((g + 1) * split + groups - 1) / groups - 1;
-}
 
 template <typename T, int BT, int TN, int STAGES, bool WMN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -211,7 +206,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     issue_w(i);
     issue_a(i);
   };
-
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       ptx::mbar_init(full_bar(i), 1);
@@ -221,9 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(recv_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
-    // The owner expects one 16-byte store per (source rank, W row, owned group).
+    // The owner expects 16 bytes per (remote source rank, W row, owned
+    // group); its own partial is read in place.
     if (split > 1) {
-      ptx::mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(split) * TN *
+      ptx::mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(split - 1) * TN *
                                                static_cast<uint32_t>(own_width) * 16u);
     }
     ptx::prefetch_tensormap(&tmap_w);
@@ -392,9 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 4; ++h) {
           const int g = 4 * q + h;
           if (g < groups) {
-            const int owner = group_owner(g, groups, split);
-            const int g_lo = (owner * groups) / split;
-            const int width = ((owner + 1) * groups) / split - g_lo;
             // [group][row]: consecutive threads (rows) write consecutive 16 B.
             uint4* dst = reinterpret_cast<uint4*>(smem + args.stage_offset) + (g * TN + n_local);
             *dst = make_uint4(r[4 * h], r[4 * h + 1], r[4 * h + 2], r[4 * h + 3]);
@@ -414,32 +406,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::fence_proxy_async_smem();
     __syncthreads();
-    if (threadIdx.x == 0 && !aborted) {
-      for (int owner = 0; owner < split; ++owner) {
-        const int g_lo = (owner * groups) / split;
-        const int width = ((owner + 1) * groups) / split - g_lo;
-        if (width > 0) {
-          const uint32_t bytes = static_cast<uint32_t>(TN * width) * 16u;
-          ptx::bulk_copy_to_peer(ptx::map_to_rank(recv + static_cast<uint32_t>(s) * bytes, static_cast<uint32_t>(owner)),
-                                 stage_out + static_cast<uint32_t>(g_lo * TN) * 16u, bytes,
-                                 ptx::map_to_rank(recv_bar, static_cast<uint32_t>(owner)));
-        }
+    // Lane d of warp 0 ships this rank's groups of owner (s + d) % split, so
+    // the copies enter the engine together and every owner is fed by a
+    // different source at any moment.
+    if (warp == 0 && lane >= 1 && lane < split && !aborted) {
+      const int owner = (s + lane) % split;
+      const int g_lo = (owner * groups) / split;
+      const int width = ((owner + 1) * groups) / split - g_lo;
+      if (width > 0) {
+        const uint32_t bytes = static_cast<uint32_t>(TN * width) * 16u;
+        // Owner's receive slot for source s: the S - 1 remote sources in rank order.
+        const uint32_t slot = static_cast<uint32_t>(s < owner ? s : s - 1);
+        ptx::bulk_copy_to_peer(ptx::map_to_rank(recv + slot * bytes, static_cast<uint32_t>(owner)),
+                               stage_out + static_cast<uint32_t>(g_lo * TN) * 16u, bytes,
+                               ptx::map_to_rank(recv_bar, static_cast<uint32_t>(owner)));
       }
     }
     const bool received = ptx::mbar_wait_bounded(recv_bar, 0u, aborted ? abort_flag : nullptr, kWaitBudgetNs);
     if (!received && !aborted) raise(kErrTimeoutEpilogue);
+    // Phase 2: a CTA arrives once its own receive barrier has completed, so
+    // passing the wait (after the stores below) means every copy of the
+    // cluster has landed and no CTA leaves while a copy from or to it is in
+    // flight.  Relaxed: the barrier orders nothing else (the receive barrier
+    // already did).
+    ptx::cluster_arrive_relaxed();
     if (received && !aborted) {
       const float4* rv = reinterpret_cast<const float4*>(smem + args.recv_offset);
+      const float4* own = reinterpret_cast<const float4*>(smem + args.stage_offset) + own_lo * TN;
       // Thread t reduces W row t % TN (its epilogue row) for owned groups
-      // j = t / TN, t / TN + 256 / TN, ...
+      // j = t / TN, t / TN + 256 / TN, ...; this rank's own partial is read
+      // from its staging buffer, the others from the receive slots.
       for (int j = threadIdx.x / TN; j < own_width; j += kThreads / TN) {
+        // All loads first (independent), then the sum in split order.
+        float4 part[GLQ_MAX_SPLIT];
+#pragma unroll
+        for (int src = 0; src < GLQ_MAX_SPLIT; ++src) {
+          if (src < split) {
+            const int slot = src < s ? src : src - 1;
+            part[src] = src == s ? own[j * TN + n_local] : rv[(slot * own_width + j) * TN + n_local];
+          }
+        }
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int src = 0; src < split; ++src) {
-          const float4 v = rv[(src * own_width + j) * TN + n_local];
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
+#pragma unroll
+        for (int src = 0; src < GLQ_MAX_SPLIT; ++src) {
+          if (src < split) {
+            acc.x += part[src].x;
+            acc.y += part[src].y;
+            acc.z += part[src].z;
+            acc.w += part[src].w;
+          }
         }
         const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
         const int mm0 = 4 * (own_lo + j);
@@ -452,11 +467,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    // Phase 2: a CTA arrives once its own receive barrier has completed, so
-    // passing the wait means every copy of the cluster has landed and no CTA
-    // leaves while a copy from or to it is in flight.  Relaxed: the barrier
-    // orders nothing else (the receive barrier already did).
-    ptx::cluster_arrive_relaxed();
     ptx::cluster_wait();
   }
 
@@ -527,8 +537,8 @@ cudaError_t set_attrs_all() {
   cudaError_t e;
   if ((e = set_attrs<T, 16, 256, 4>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 32, 256, 4>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 16, 128, 5>()) != cudaSuccess) return e;
-  if ((e = set_attrs<T, 32, 128, 5>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 16, 128, kPairStages>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 32, 128, kPairStages>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 16, 128, 8>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 32, 128, 8>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 64, 128, 8>()) != cudaSuccess) return e;
@@ -569,7 +579,8 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   args.err = err;
   args.flags = p.flags;
   // Shared memory: [pipeline stages][split-K receive buffer][mbarriers].
-  // The receive buffer (split x TN rows x owned groups x 16 B) gets its own
+  // The receive buffer ((split - 1) remote sources x TN rows x owned groups
+  // x 16 B) gets its own
   // region when it fits; otherwise it reuses the drained stages, after one
   // more cluster barrier.  The send staging buffer (TN rows x all groups x
   // 16 B) always reuses the drained stages, after the receive buffer.
@@ -577,11 +588,12 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   if (split > 1) {
     const uint32_t groups = BT / 4;
     const uint32_t width = (groups + split - 1) / split;
-    recv_bytes = static_cast<uint32_t>(split) * TN * width * 16u;
+    recv_bytes = static_cast<uint32_t>(split - 1) * TN * width * 16u;
     stage_bytes = TN * groups * 16u;
   }
-  // The 5-stage ring is the two-CTAs-per-SM configuration: keep under half an SM.
-  const uint32_t budget = STAGES == 5 ? kPairSmemBudget : kSmemLimit;
+  // The two-CTAs-per-SM configuration keeps under half an SM.
+  constexpr bool kPair = TN == 128 && BT <= 32 && STAGES == kPairStages;
+  const uint32_t budget = kPair ? kPairSmemBudget : kSmemLimit;
   const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= budget;
   args.recv_offset = dedicated ? Cfg::kPipeBytes : 0;
   args.stage_offset = dedicated ? 0 : ((recv_bytes + 1023u) & ~1023u);
@@ -620,10 +632,10 @@ cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int s
       default: return cudaErrorInvalidValue;
     }
   }
-  if (stages == 5) {
+  if (stages == kPairStages) {
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 128, 5, WMN>(p, split, err, s);
-      case 32: return launch_typed<T, 32, 128, 5, WMN>(p, split, err, s);
+      case 16: return launch_typed<T, 16, 128, kPairStages, WMN>(p, split, err, s);
+      case 32: return launch_typed<T, 32, 128, kPairStages, WMN>(p, split, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
