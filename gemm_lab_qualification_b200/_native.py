@@ -24,6 +24,7 @@ STATUS_OK = 0
 STATUS_NAMES = ("ok", "invalid_argument", "shape", "split", "workspace", "output_layout", "cuda",
                 "device", "device_timeout")
 MAX_SPLIT = 8
+MAX_RANKS = 8
 FLAG_NO_PDL = 1 << 0
 FLAG_STATIC_WEIGHTS = 1 << 1
 
@@ -41,6 +42,9 @@ SIGNATURES = {
                               _INT, _VP, ctypes.c_size_t, _VP, _PINT]),
     "glq_matmul": (_INT, [_INT, _VP, _VP, _VP, _INT, _INT, _INT, _VP]),
     "glq_splitk_matmul": (_INT, [_INT, _VP, _VP, _VP, _INT, _INT, _INT, _VP, _INT, _VP]),
+    "glq_linear_gather": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _VP, _INT, ctypes.POINTER(_VP), _I64,
+                                 _I64, _I64, _I64, _I64, _INT, _INT, _INT, ctypes.POINTER(_VP),
+                                 ctypes.POINTER(ctypes.c_uint), ctypes.c_uint64, _VP, ctypes.c_uint, _PINT, _PINT]),
     "glq_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _INT]),
     "glq_plan": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _INT,
                         _PINT, _PINT]),
@@ -148,6 +152,38 @@ def linear(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, bias: torch.Tens
         ctypes.byref(path), ctypes.byref(split))
     if status != STATUS_OK:
         raise GlqError(status, "glq_linear_ex")
+    return PATHS[path.value], split.value
+
+
+def linear_gather(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None, epilogue: int,
+                  y_ptrs: list[int], y_row_stride: int, y_col_offset: int, rank: int,
+                  signal_ptrs: list[int], counter_ptr: int, epoch: int, split_k: int = 0,
+                  stream: torch.cuda.Stream | None = None, flags: int = 0) -> tuple[str, int]:
+    """One rank's column-parallel linear with the all-gather fused in (glq_linear_gather).
+
+    y_ptrs / signal_ptrs: per rank, device pointers mapped in this process to
+    that rank's output buffer and signal slots; this rank's N columns land at
+    y_col_offset in every rank's buffer.  Returns (path, split).
+    """
+    m, k = a.shape
+    n = b.shape[1]
+    world = len(y_ptrs)
+    if stream is None:
+        stream = torch.cuda.current_stream(a.device)
+    ys = (_VP * world)(*y_ptrs)
+    sigs = (_VP * world)(*signal_ptrs)
+    path = ctypes.c_int(-1)
+    split = ctypes.c_int(0)
+    status = library().glq_linear_gather(
+        dtype_code(a.dtype),
+        a.data_ptr(), a.stride(0), a.stride(1),
+        b.data_ptr(), b.stride(0), b.stride(1),
+        bias.data_ptr() if bias is not None else None, epilogue,
+        ys, y_row_stride, y_col_offset, m, n, k, split_k, rank, world,
+        sigs, ctypes.cast(ctypes.c_void_p(counter_ptr), ctypes.POINTER(ctypes.c_uint)), epoch,
+        stream.cuda_stream, flags, ctypes.byref(path), ctypes.byref(split))
+    if status != STATUS_OK:
+        raise GlqError(status, "glq_linear_gather")
     return PATHS[path.value], split.value
 
 

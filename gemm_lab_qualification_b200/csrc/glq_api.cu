@@ -129,7 +129,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
     return GLQ_OK;
   }
   c->w_mn = w_mnmajor ? 1 : 0;
-  if (p.m == 1 && w_kmajor) {
+  if (p.m == 1 && w_kmajor && !p.require_tc) {
     c->kernel = kKernelGemv;
     c->split = split_k > 0 ? split_k : 1;
     c->path = (p.k % 8 != 0) ? GLQ_PATH_TAIL : GLQ_PATH_GEMV_M1;
@@ -258,7 +258,8 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
     case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
-    case glq::kKernelTc: e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, dev->error_word, s);
+    case glq::kKernelTc:
+      e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, nullptr, dev->error_word, s);
       break;
     case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
     default: break;
@@ -269,6 +270,73 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   }
   if (path_out) *path_out = c.path;
   if (split_out) *split_out = c.kernel == glq::kKernelGeneric ? 1 : c.split;
+  return GLQ_OK;
+}
+
+int glq_linear_gather(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride, const void* B,
+                      int64_t b_k_stride, int64_t b_n_stride, const void* bias, int epilogue, void* const* y_ranks,
+                      int64_t y_row_stride, int64_t y_col_offset, int64_t M, int64_t N, int64_t K, int split_k,
+                      int rank, int world, uint64_t* const* signal_ranks, unsigned int* counter, uint64_t epoch,
+                      void* stream, unsigned int flags, int* path_out, int* split_out) {
+  int v = glq::validate(dtype, epilogue, M, N, K, split_k);
+  if (v != GLQ_OK) return v;
+  if ((flags & ~(GLQ_FLAG_NO_PDL | GLQ_FLAG_STATIC_WEIGHTS)) != 0) return GLQ_ERR_INVALID_ARGUMENT;
+  if (world < 1 || world > GLQ_MAX_RANKS || rank < 0 || rank >= world) return GLQ_ERR_INVALID_ARGUMENT;
+  if (M <= 0 || N <= 0 || K <= 0) return GLQ_ERR_SHAPE;
+  if (A == nullptr || B == nullptr || y_ranks == nullptr || signal_ranks == nullptr || counter == nullptr ||
+      epoch == 0) {
+    return GLQ_ERR_INVALID_ARGUMENT;
+  }
+  if (epilogue != GLQ_EPILOGUE_NONE && bias == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
+  if (y_col_offset < 0 || y_row_stride < y_col_offset + N) return GLQ_ERR_OUTPUT_LAYOUT;
+  constexpr int64_t esz = 2;
+  glq::Gather g = {};
+  g.rank = rank;
+  g.world = world;
+  for (int r = 0; r < world; ++r) {
+    if (y_ranks[r] == nullptr || signal_ranks[r] == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
+    g.y[r] = static_cast<char*>(y_ranks[r]) + y_col_offset * esz;
+    g.signal[r] = reinterpret_cast<unsigned long long*>(signal_ranks[r]);
+  }
+  g.counter = counter;
+  g.epoch = static_cast<unsigned long long>(epoch);
+
+  Problem p = {};
+  p.dtype = dtype;
+  p.a = A;
+  p.a_rs = a_row_stride;
+  p.a_cs = a_col_stride;
+  p.b = B;
+  p.b_ks = b_k_stride;
+  p.b_ns = b_n_stride;
+  p.bias = bias;
+  p.epilogue = epilogue;
+  p.y = g.y[rank];
+  p.ldy = y_row_stride;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  p.partial = nullptr;
+  p.flags = flags;
+  p.require_tc = 1;
+
+  if (path_out) *path_out = GLQ_PATH_EMPTY;
+  if (split_out) *split_out = 1;
+  glq::DeviceState* dev = nullptr;
+  v = glq::device_state(&dev);
+  if (v != GLQ_OK) return v;
+  Choice c;
+  v = glq::plan_problem(p, split_k, dev->sm_count, &c);
+  if (v != GLQ_OK) return v;
+  if (c.kernel != glq::kKernelTc) return GLQ_ERR_INVALID_ARGUMENT;
+  const cudaError_t e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, &g, dev->error_word,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_CUDA;
+  }
+  if (path_out) *path_out = c.path;
+  if (split_out) *split_out = c.split;
   return GLQ_OK;
 }
 

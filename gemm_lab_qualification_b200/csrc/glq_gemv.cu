@@ -127,12 +127,29 @@ __global__ void __launch_bounds__(kBlockThreadsMax, 4) gemv_kernel(const GemvArg
   if (static_w) load_w(c_begin + lane);
   ptx::grid_dependency_wait();
   ptx::grid_launch_dependents();
-  // First weight chunks in flight before anything else, then A staged once
-  // per block in shared memory (every warp reads all of A), then the bias of
-  // this warp's row, so none of these latencies lands at the end.
+  // A (a few KB, resident in L2) is requested first so that its loads do not
+  // queue behind the weight stream, then the first weight chunks; A is staged
+  // once per block in shared memory (every warp reads all of it), then the
+  // bias of this warp's row is requested, so none of these latencies lands at
+  // the end.
+  constexpr int kAPerThread = 2;
+  uint4 a_regs[kAPerThread];
+  int a_next = threadIdx.x;
+  if (g.a_in_smem) {
+#pragma unroll
+    for (int i = 0; i < kAPerThread; ++i) {
+      const int c = a_next + i * static_cast<int>(blockDim.x);
+      if (c < chunks) a_regs[i] = __ldg(av + c);
+    }
+  }
   if (!static_w) load_w(c_begin + lane);
   if (g.a_in_smem) {
-    for (int c = threadIdx.x; c < chunks; c += blockDim.x) a_smem[c] = __ldg(av + c);
+#pragma unroll
+    for (int i = 0; i < kAPerThread; ++i) {
+      const int c = a_next + i * static_cast<int>(blockDim.x);
+      if (c < chunks) a_smem[c] = a_regs[i];
+    }
+    for (int c = a_next + kAPerThread * static_cast<int>(blockDim.x); c < chunks; c += blockDim.x) a_smem[c] = __ldg(av + c);
   }
   float bias_v = 0.0f;
   if (g.epilogue != GLQ_EPILOGUE_NONE && row_ok && part == 0 && lane == 0) {

@@ -19,6 +19,7 @@ enum DeviceErrorBits : unsigned int {
   kErrTimeoutEpilogue = 1u << 2,  // epilogue gave up waiting for the accumulator
   kErrTimeoutDrain = 1u << 3,     // in-flight TMA loads did not land at exit
   kErrSmemAlign = 1u << 4,        // dynamic shared memory not 1024-B aligned
+  kErrTimeoutPeer = 1u << 5,      // a peer rank never published its gathered slice
 };
 
 // Time budget of one bounded in-kernel wait.  Legitimate waits last
@@ -39,6 +40,18 @@ struct Problem {
   int64_t m, n, k;
   float* partial;  // optional [split, m, n] FP32 split partials
   unsigned int flags;  // glq_flags
+  int require_tc;      // 1: the tcgen05 kernel or an error (fused gather)
+};
+
+// Fused all-gather of a column-parallel layer (glq_linear_gather): output
+// bases already offset to this rank's first column, and the completion
+// protocol's signal slots.
+struct Gather {
+  int rank, world;
+  void* y[GLQ_MAX_RANKS];
+  unsigned long long* signal[GLQ_MAX_RANKS];
+  unsigned int* counter;
+  unsigned long long epoch;
 };
 
 // Path selection result.
@@ -98,8 +111,9 @@ cudaError_t launch_gemv(const Problem& p, int split, unsigned int* err, cudaStre
 cudaError_t launch_generic(const Problem& p, cudaStream_t s);
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
+// gather: null for a plain call (the output is p.y only).
 cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
-                      unsigned int* err, cudaStream_t s);
+                      const Gather* gather, unsigned int* err, cudaStream_t s);
 
 // Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).
 cudaError_t tc_prepare_device();

@@ -83,6 +83,18 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilo
   return __fdividef(v, 1.0f + __expf(-v));  // SiLU = v * sigmoid(v)
 }
 
+// One output element to every output buffer of the call (this rank's own Y,
+// and with a fused gather every peer's Y over NVLink), starting with a
+// different buffer per tile so the peers' links are loaded evenly.
+template <typename T, typename Args>
+__device__ __forceinline__ void store_out(const Args& args, long long offset, T v, int first) {
+  for (int i = 0; i < args.n_out; ++i) {
+    int o = first + i;
+    if (o >= args.n_out) o -= args.n_out;
+    static_cast<T*>(args.y_out[o])[offset] = v;
+  }
+}
+
 constexpr int kTileK = 64;  // K elements per stage: one 128-byte swizzle row
 constexpr uint32_t kMnBoxBytes = 64u * kTileK * 2u;  // one 64(n) x 64(k) MN-major W box
 constexpr int kThreads = 256;
@@ -120,10 +132,18 @@ struct TcArgs {
   int split;
   int epilogue;
   const void* bias;
-  void* y;
+  void* y_out[GLQ_MAX_RANKS];  // output bases (this rank's columns); [0] alone unless gathering
+  int n_out;
   long long ldy;
   float* partial;
   unsigned int* err;
+  // Fused gather completion (counter == nullptr: plain call).
+  unsigned long long* sig_out[GLQ_MAX_RANKS];  // every rank's signal slots
+  unsigned long long* sig_in;                  // this rank's signal slots
+  unsigned int* counter;
+  unsigned long long epoch;
+  int rank;
+  uint32_t ys_offset;  // fused gather: FP16 output tile staging (bytes from the aligned base); ~0u = none
   uint32_t recv_offset;     // split-K receive buffer, bytes from the 1024-aligned base
   uint32_t stage_offset;    // split-K send staging buffer (inside the drained pipeline)
   int recv_overlaps;        // 1: the receive buffer reuses the drained pipeline stages
@@ -131,7 +151,7 @@ struct TcArgs {
   unsigned int flags;       // glq_flags
 };
 
-template <typename T, int BT, int TN, int STAGES, bool WMN>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_a, const TcArgs args) {
@@ -342,7 +362,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after_sync();
 
   const int chunks = (mr + 15) >> 4;
-  T* y = static_cast<T*>(args.y);
+  // Output stores: this rank's Y directly; with a fused gather the FP16
+  // tile is first staged in shared memory as [token][W row] (the drained
+  // pipeline), then written to every rank's Y as 16-byte vectors (one
+  // NVLink-friendly store per 8 outputs instead of eight 2-byte ones).
+  T* const y = static_cast<T*>(args.y_out[0]);
+  const int out_first = GATHER ? static_cast<int>((blockIdx.y + blockIdx.z) % static_cast<unsigned>(args.n_out)) : 0;
+  const bool stage_out = GATHER && args.ys_offset != ~0u;
+  T* const ys = reinterpret_cast<T*>(smem + (stage_out ? args.ys_offset : 0u));
+  // mm: token within this CTA's token tile; mm_base: first token of the staged rows.
+  auto store = [&](int mm, int mm_base, T v) {
+    if constexpr (GATHER) {
+      if (stage_out) {
+        ys[(mm - mm_base) * TN + n_local] = v;
+      } else {
+        store_out<T>(args, (m0 + mm) * args.ldy + n, v, out_first);
+      }
+    } else {
+      y[(m0 + mm) * args.ldy + n] = v;
+    }
+  };
+  // Staged rows [mm_base, mm_base + rows) of the tile to every output.
+  auto flush_staged = [&](int mm_base, int rows) {
+    if constexpr (GATHER) {
+      if (!stage_out) return;
+      __syncthreads();
+      constexpr int kVec = 8;                // FP16/BF16 outputs per 16-byte store
+      constexpr int kChunks = TN / kVec;
+      const long long n_tile = static_cast<long long>(tile_n) * TN;
+      for (int idx = threadIdx.x; idx < rows * kChunks; idx += kThreads) {
+        const int row = idx / kChunks;
+        const int c = idx - row * kChunks;
+        const long long n0 = n_tile + c * kVec;
+        const long long off = (m0 + mm_base + row) * args.ldy + n0;
+        const T* src = ys + row * TN + c * kVec;
+        if (n0 + kVec <= args.n) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src);
+          for (int i = 0; i < args.n_out; ++i) {
+            int o = out_first + i;
+            if (o >= args.n_out) o -= args.n_out;
+            *reinterpret_cast<uint4*>(static_cast<T*>(args.y_out[o]) + off) = v;
+          }
+        } else {
+          for (int e = 0; e < kVec && n0 + e < args.n; ++e) store_out<T>(args, off + e, src[e], out_first);
+        }
+      }
+    }
+  };
   const uint32_t t_row =
       tmem_d + (static_cast<uint32_t>(lane_group * 32) << 16) + static_cast<uint32_t>(acc_idx * BT);
 
@@ -356,12 +422,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 16; ++j) {
           const int mm = q * 16 + j;
           if (mm < mr && n_ok) {
-            y[(m0 + mm) * args.ldy + n] =
-                Elem<T>::from_f(apply_epilogue(__uint_as_float(r[j]), bias_v, args.epilogue));
+            store(mm, 0, Elem<T>::from_f(apply_epilogue(__uint_as_float(r[j]), bias_v, args.epilogue)));
           }
         }
       }
     }
+    flush_staged(0, aborted ? 0 : mr);
   } else {
     // Split-K merge.  Every CTA stages its FP32 partial tile in its own
     // drained pipeline memory as [group][row] (16 bytes per entry, so
@@ -462,11 +528,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) {
           const int mm = mm0 + c;
           if (mm < mr && n_ok) {
-            y[(m0 + mm) * args.ldy + n] = Elem<T>::from_f(apply_epilogue(vals[c], bias_v, args.epilogue));
+            store(mm, 4 * own_lo, Elem<T>::from_f(apply_epilogue(vals[c], bias_v, args.epilogue)));
           }
         }
       }
     }
+    flush_staged(4 * own_lo, (received && !aborted) ? max(0, min(4 * own_width, mr - 4 * own_lo)) : 0);
     ptx::cluster_wait();
   }
 
@@ -486,6 +553,57 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     ptx::tc_fence_after_sync();
     ptx::tmem_dealloc(tmem_d, Cfg::kTmemCols);
+  }
+
+  // ---- Fused gather completion.  After the CTA barrier, thread 0 fences
+  // at GPU scope (cumulative over the CTA's stores, local and peer) and
+  // counts the CTA in with a fire-and-forget add: a release pattern that
+  // CTA 0's acquire pattern (relaxed poll, then fence) synchronises with on
+  // this GPU.  CTA 0 of the grid waits until every CTA has counted in,
+  // resets the counter, fences at system scope (so every CTA's stores
+  // precede, in causality order, what follows), writes the epoch into this
+  // rank's slot of every rank's signal array and waits, bounded, until every
+  // rank has written its slot here, reading the slots with system-scope
+  // acquire loads (which order the peers' slices before the kernel's end).
+  // Only CTA 0 pays a system-scope fence: hundreds of concurrent ones
+  // serialise.  The kernel therefore completes only when this rank's output
+  // holds all slices.  Every wait is bounded; on expiry the device error
+  // word gets kErrTimeoutPeer and the kernel returns.
+  if constexpr (GATHER) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      ptx::fence_acq_rel_gpu();
+      ptx::red_add_relaxed_gpu(args.counter, 1u);
+      if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+        const uint64_t t0 = ptx::globaltimer_ns();
+        bool ok = true;
+        uint32_t polls = 0;
+        auto expired = [&]() {
+          return (++polls & 63u) == 0u && (ptx::globaltimer_ns() - t0 > kWaitBudgetNs || polls > (1u << 26));
+        };
+        while (ptx::ld_relaxed_gpu_u32(args.counter) < total) {
+          if (expired()) {
+            ok = false;
+            break;
+          }
+        }
+        if (ok) {
+          *args.counter = 0u;  // every CTA of this grid has counted in
+          ptx::fence_acq_rel_sys();
+          for (int r = 0; r < args.n_out; ++r) ptx::st_relaxed_sys_u64(args.sig_out[r] + args.rank, args.epoch);
+          for (int r = 0; r < args.n_out && ok; ++r) {
+            while (ptx::ld_acquire_sys_u64(args.sig_in + r) < args.epoch) {
+              if (expired()) {
+                ok = false;
+                break;
+              }
+            }
+          }
+        }
+        if (!ok) atomicOr(args.err, kErrTimeoutPeer);
+      }
+    }
   }
 }
 
@@ -523,13 +641,19 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   return r == CUDA_SUCCESS;
 }
 
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER>
+cudaError_t set_attr() {
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
+}
+
 template <typename T, int BT, int TN, int STAGES>
 cudaError_t set_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, true>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
+  cudaError_t e;
+  if ((e = set_attr<T, BT, TN, STAGES, false, false>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, BT, TN, STAGES, true, false>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, BT, TN, STAGES, false, true>()) != cudaSuccess) return e;
+  return set_attr<T, BT, TN, STAGES, true, true>();
 }
 
 template <typename T>
@@ -546,8 +670,8 @@ cudaError_t set_attrs_all() {
   return set_attrs<T, 256, 128, 4>();
 }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN>
-cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStream_t stream) {
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER>
+cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
   CUtensorMap tmap_w, tmap_a;
   const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
@@ -573,7 +697,24 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   args.split = split;
   args.epilogue = p.epilogue;
   args.bias = p.bias;
-  args.y = p.y;
+  args.n_out = 1;
+  args.y_out[0] = p.y;
+  args.counter = nullptr;
+  args.sig_in = nullptr;
+  args.epoch = 0;
+  args.rank = 0;
+  for (int r = 0; r < GLQ_MAX_RANKS; ++r) args.sig_out[r] = nullptr;
+  if (g != nullptr) {
+    args.n_out = g->world;
+    for (int r = 0; r < g->world; ++r) {
+      args.y_out[r] = g->y[r];
+      args.sig_out[r] = g->signal[r];
+    }
+    args.sig_in = g->signal[g->rank];
+    args.counter = g->counter;
+    args.epoch = g->epoch;
+    args.rank = g->rank;
+  }
   args.ldy = p.ldy;
   args.partial = p.partial;
   args.err = err;
@@ -599,6 +740,17 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   args.stage_offset = dedicated ? 0 : ((recv_bytes + 1023u) & ~1023u);
   args.recv_overlaps = dedicated ? 0 : 1;
   if (args.stage_offset + stage_bytes > Cfg::kPipeBytes) return cudaErrorInvalidValue;
+  // Fused gather: the FP16 output tile is staged in the drained pipeline,
+  // after the split-K buffers (16-byte rows need 16-byte aligned outputs).
+  args.ys_offset = ~0u;
+  if (GATHER && (p.ldy * esz) % 16 == 0 && g != nullptr) {
+    bool bases_ok = true;
+    for (int r = 0; r < g->world; ++r) bases_ok = bases_ok && (reinterpret_cast<uintptr_t>(g->y[r]) % 16 == 0);
+    const uint32_t used = split > 1 ? (dedicated ? stage_bytes : args.stage_offset + stage_bytes) : 0u;
+    const uint32_t ys_off = (used + 15u) & ~15u;
+    const uint32_t rows = split > 1 ? 4u * ((BT / 4 + split - 1) / split) : static_cast<uint32_t>(BT);
+    if (bases_ok && ys_off + rows * TN * static_cast<uint32_t>(esz) <= Cfg::kPipeBytes) args.ys_offset = ys_off;
+  }
   const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : Cfg::kPipeBytes;
   args.barrier_offset = (body + 15u) & ~15u;
   const uint32_t smem_bytes = 1024 + args.barrier_offset + Cfg::kBarrierBytes;
@@ -619,32 +771,32 @@ cudaError_t launch_typed(const Problem& p, int split, unsigned int* err, cudaStr
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN>, tmap_w, tmap_a, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER>, tmap_w, tmap_a, args);
 }
 
-template <typename T, bool WMN>
-cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
-                      cudaStream_t s) {
+template <typename T, bool WMN, bool GATHER>
+cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, const Gather* g,
+                      unsigned int* err, cudaStream_t s) {
   if (tile_n == 256) {
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 256, 4, WMN>(p, split, err, s);
-      case 32: return launch_typed<T, 32, 256, 4, WMN>(p, split, err, s);
+      case 16: return launch_typed<T, 16, 256, 4, WMN, GATHER>(p, split, g, err, s);
+      case 32: return launch_typed<T, 32, 256, 4, WMN, GATHER>(p, split, g, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
   if (stages == kPairStages) {
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 128, kPairStages, WMN>(p, split, err, s);
-      case 32: return launch_typed<T, 32, 128, kPairStages, WMN>(p, split, err, s);
+      case 16: return launch_typed<T, 16, 128, kPairStages, WMN, GATHER>(p, split, g, err, s);
+      case 32: return launch_typed<T, 32, 128, kPairStages, WMN, GATHER>(p, split, g, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (tile_t) {
-    case 16: return launch_typed<T, 16, 128, 8, WMN>(p, split, err, s);
-    case 32: return launch_typed<T, 32, 128, 8, WMN>(p, split, err, s);
-    case 64: return launch_typed<T, 64, 128, 8, WMN>(p, split, err, s);
-    case 128: return launch_typed<T, 128, 128, 6, WMN>(p, split, err, s);
-    case 256: return launch_typed<T, 256, 128, 4, WMN>(p, split, err, s);
+    case 16: return launch_typed<T, 16, 128, 8, WMN, GATHER>(p, split, g, err, s);
+    case 32: return launch_typed<T, 32, 128, 8, WMN, GATHER>(p, split, g, err, s);
+    case 64: return launch_typed<T, 64, 128, 8, WMN, GATHER>(p, split, g, err, s);
+    case 128: return launch_typed<T, 128, 128, 6, WMN, GATHER>(p, split, g, err, s);
+    case 256: return launch_typed<T, 256, 128, 4, WMN, GATHER>(p, split, g, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -658,13 +810,21 @@ cudaError_t tc_prepare_device() {
 }
 
 cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
-                      unsigned int* err, cudaStream_t s) {
-  if (p.dtype == GLQ_DTYPE_BF16) {
-    return w_mn ? launch_bt<__nv_bfloat16, true>(p, split, tile_t, tile_n, stages, err, s)
-                : launch_bt<__nv_bfloat16, false>(p, split, tile_t, tile_n, stages, err, s);
+                      const Gather* g, unsigned int* err, cudaStream_t s) {
+  if (g != nullptr) {
+    if (p.dtype == GLQ_DTYPE_BF16) {
+      return w_mn ? launch_bt<__nv_bfloat16, true, true>(p, split, tile_t, tile_n, stages, g, err, s)
+                  : launch_bt<__nv_bfloat16, false, true>(p, split, tile_t, tile_n, stages, g, err, s);
+    }
+    return w_mn ? launch_bt<__half, true, true>(p, split, tile_t, tile_n, stages, g, err, s)
+                : launch_bt<__half, false, true>(p, split, tile_t, tile_n, stages, g, err, s);
   }
-  return w_mn ? launch_bt<__half, true>(p, split, tile_t, tile_n, stages, err, s)
-              : launch_bt<__half, false>(p, split, tile_t, tile_n, stages, err, s);
+  if (p.dtype == GLQ_DTYPE_BF16) {
+    return w_mn ? launch_bt<__nv_bfloat16, true, false>(p, split, tile_t, tile_n, stages, g, err, s)
+                : launch_bt<__nv_bfloat16, false, false>(p, split, tile_t, tile_n, stages, g, err, s);
+  }
+  return w_mn ? launch_bt<__half, true, false>(p, split, tile_t, tile_n, stages, g, err, s)
+              : launch_bt<__half, false, false>(p, split, tile_t, tile_n, stages, g, err, s);
 }
 
 }  // namespace glq

@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define GLQ_ABI_VERSION 1
+#define GLQ_ABI_VERSION 2
 
 /* Element types (inputs, bias and output share one type). */
 enum glq_dtype {
@@ -203,6 +203,49 @@ int glq_plan(int dtype,
              const void* B, int64_t b_k_stride, int64_t b_n_stride,
              int64_t y_row_stride, int64_t M, int64_t N, int64_t K,
              int split_k, int sm_count, int* path_out, int* split_out);
+
+/* Ranks one fused-gather call can address. */
+#define GLQ_MAX_RANKS 8
+
+/*
+ * glq_linear_gather -- one rank's share of a column-parallel (N-sharded)
+ * linear layer with the all-gather fused into the kernel's epilogue.  This
+ * rank computes Y_r = epilogue(A . B_r) for its N-slice exactly as glq_linear
+ * does (same planner, tensor-core paths only), and the epilogue stores every
+ * output element straight into all `world` ranks' output buffers over
+ * NVLink (plain peer stores; no TMA multicast, no library kernel touches
+ * peer memory).  The last CTA to finish then publishes `epoch` into slot
+ * [rank] of every rank's signal array and waits (bounded) until all `world`
+ * slots of its own array reached `epoch`; when the kernel completes, this
+ * rank's output buffer holds every rank's slice.
+ *
+ * y_ranks[r]      device pointer (mapped in this process) to rank r's output
+ *                 [M, N * world] row-major buffer, row pitch y_row_stride;
+ *                 this rank writes columns [y_col_offset, y_col_offset + N).
+ * signal_ranks[r] device pointer (mapped in this process) to rank r's array
+ *                 of `world` uint64 slots, zero-initialised once.
+ * counter         this rank's device arrival counter, zero before the first
+ *                 call; every call leaves it zero.
+ * epoch           strictly larger than the previous call's, equal on all
+ *                 ranks for the same call.
+ * Requires K > 0 and operands the tensor-core paths take (K-contiguous or
+ * N-contiguous B, 16-byte aligned); otherwise GLQ_ERR_INVALID_ARGUMENT.  A
+ * peer that never publishes sets a bit in the device error word
+ * (glq_device_error) after the wait budget; the kernel still returns.
+ *
+ * No reference counterpart: the reference has no multi-GPU path.  It
+ * replaces the local GEMM followed by an NCCL all_gather_into_tensor and
+ * the [P, M, N/P] -> [M, N] layout copy of the column-parallel layer.
+ */
+int glq_linear_gather(int dtype,
+                      const void* A, int64_t a_row_stride, int64_t a_col_stride,
+                      const void* B, int64_t b_k_stride, int64_t b_n_stride,
+                      const void* bias, int epilogue,
+                      void* const* y_ranks, int64_t y_row_stride, int64_t y_col_offset,
+                      int64_t M, int64_t N, int64_t K, int split_k,
+                      int rank, int world,
+                      uint64_t* const* signal_ranks, unsigned int* counter, uint64_t epoch,
+                      void* stream, unsigned int flags, int* path_out, int* split_out);
 
 /* Names of paths and statuses (static strings, never NULL). */
 const char* glq_path_name(int path);

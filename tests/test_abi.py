@@ -42,7 +42,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_abi_version_and_target():
     lib = native.library()
-    assert lib.glq_abi_version() == 1
+    assert lib.glq_abi_version() == 2
     assert lib.glq_build_target() == b"sm_100a"
 
 
@@ -223,3 +223,42 @@ def test_adaptive_path_names_native_kernel():
     # MLP up-projection: 43 tiles of 256 rows, split 3 -> 129 CTAs.
     assert kernels.adaptive_bias_silu_path(8, 11008, 4096, torch.float16) == "tc_splitk"
     assert kernels.adaptive_path(8, 11008, 4096, torch.float16) == "tc_splitk"
+
+
+def gather_status(**over):
+    """glq_linear_gather with plausible host-side arguments; pointers are fake
+    (non-null) because every check below fails before any device access."""
+    lib = native.library()
+    VP = ctypes.c_void_p
+    args = dict(dtype=0, a=16, lda=4096, acs=1, b=16, bks=1, bns=4096, bias=16, epi=2, ldy=8192, off=4096,
+                m=32, n=4096, k=4096, split=0, rank=1, world=2, counter=16, epoch=1, flags=0)
+    args.update(over)
+    ys = (VP * 2)(16, 16) if over.get("ys", True) else None
+    sigs = (VP * 2)(16, 16) if over.get("sigs", True) else None
+    counter = ctypes.cast(VP(args["counter"]), ctypes.POINTER(ctypes.c_uint)) if args["counter"] else None
+    return lib.glq_linear_gather(args["dtype"], args["a"], args["lda"], args["acs"], args["b"], args["bks"],
+                                 args["bns"], args["bias"], args["epi"], ys, args["ldy"], args["off"], args["m"],
+                                 args["n"], args["k"], args["split"], args["rank"], args["world"], sigs, counter,
+                                 args["epoch"], None, args["flags"], None, None)
+
+
+def test_gather_argument_validation():
+    assert gather_status(world=0) == 1
+    assert gather_status(world=9) == 1
+    assert gather_status(rank=2) == 1
+    assert gather_status(rank=-1) == 1
+    assert gather_status(epoch=0) == 1
+    assert gather_status(counter=0) == 1
+    assert gather_status(ys=False) == 1
+    assert gather_status(sigs=False) == 1
+    assert gather_status(a=0) == 1
+    assert gather_status(bias=0) == 1
+    assert gather_status(flags=4) == 1
+    assert gather_status(m=0) == 2
+    assert gather_status(k=0) == 2
+    assert gather_status(split=9) == 3
+    assert gather_status(ldy=8000) == 5      # y_col_offset + N > row pitch
+    assert gather_status(off=-1) == 5
+    # valid arguments reach the device check: no sm_100a GPU here
+    if not torch.cuda.is_available():
+        assert gather_status() == 7
