@@ -598,7 +598,11 @@ def run_native(args) -> int:
                             "note": "per rank: pinned host A, W slice, bias in; gathered Y out; max over ranks"},
                     "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                                  "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
-                                 "note": "per-rank bytes (A, W slice, bias, gathered Y) over the mean layer call"}}
+                                 "nvlink_bytes_per_rank": 2 * m * ns * (world - 1),
+                                 "nvlink_time_us_at_770_gbs": 2 * m * ns * (world - 1) / 770e9 * 1e6,
+                                 "note": "per-rank HBM bytes (A, W slice, bias, gathered Y) over the mean layer "
+                                         "call; the NVLink leg (this rank's slice to every peer) is the smaller "
+                                         "bound at these sizes"}}
             print(json.dumps(line), flush=True)
         return 0
 

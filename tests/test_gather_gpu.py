@@ -9,7 +9,7 @@ On one GPU the protocol is driven by ONE launch whose "peer" buffers are
 local allocations: the peer's publication is either pre-set by the test
 (so the wait completes without any other kernel) or never made (so the
 bounded wait runs out and the kernel reports it in the device error word).
-No two kernels that wait on each other ever share a GPU.  The two-rank test
+No two kernels that wait on each other ever share a GPU.  The multi-rank test
 runs one process per GPU and is skipped with fewer than two GPUs.
 """
 from __future__ import annotations
@@ -165,7 +165,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _two_rank_worker(rank: int, world: int, port: int, errors) -> None:
+def _rank_worker(rank: int, world: int, port: int, errors) -> None:
     sys.path.insert(0, str(REPO))
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import datetime
@@ -179,7 +179,7 @@ def _two_rank_worker(rank: int, world: int, port: int, errors) -> None:
         from oracle import reference as orc
         expected = None
         for m in (32, 1):
-            a, w, bias = wl.uniform_inputs(m, 4096, 4096)
+            a, w, bias = wl.uniform_inputs(m, 1024 * world, 4096)
             layer = sharded.ColumnParallelLinear(w, bias, "silu", device=dev, fused_gather=True, max_rows=m)
             da = a.to(dev)
             outs = [layer(da).clone() for _ in range(3)]
@@ -198,12 +198,16 @@ def _two_rank_worker(rank: int, world: int, port: int, errors) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_column_parallel_fused_two_gpus():
+def test_column_parallel_fused_multi_gpu():
+    """One process per visible GPU (2 to 8): the fused layer on every rank
+    equals the unsharded FP64 reference, three calls in a row (both buffer
+    parities), for M = 32 (split-K tiles) and M = 1."""
     import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     errors = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, errors)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_worker, args=(r, world, port, errors)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
