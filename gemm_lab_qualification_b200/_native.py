@@ -22,9 +22,10 @@ EPILOGUE_NONE, EPILOGUE_BIAS, EPILOGUE_BIAS_SILU = 0, 1, 2
 PATHS = ("empty", "zero_k", "gemv_m1", "tc_tcgen05", "tc_splitk", "tail", "strided", "unaligned", "tc_kn")
 STATUS_OK = 0
 STATUS_NAMES = ("ok", "invalid_argument", "shape", "split", "workspace", "output_layout", "cuda",
-                "device", "device_timeout")
+                "device", "device_timeout", "scratch")
 MAX_SPLIT = 8
 MAX_RANKS = 8
+STATIC_GATHER_SLOTS = 64
 FLAG_NO_PDL = 1 << 0
 FLAG_STATIC_WEIGHTS = 1 << 1
 
@@ -45,6 +46,9 @@ SIGNATURES = {
     "glq_linear_gather": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _VP, _INT, ctypes.POINTER(_VP), _I64,
                                  _I64, _I64, _I64, _I64, _INT, _INT, _INT, ctypes.POINTER(_VP),
                                  ctypes.POINTER(ctypes.c_uint), ctypes.c_uint64, _VP, ctypes.c_uint, _PINT, _PINT]),
+    "glq_linear_gather_static": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _VP, _INT, ctypes.POINTER(_VP),
+                                        _I64, _I64, _I64, _I64, _I64, _INT, _INT, _INT, ctypes.POINTER(_VP),
+                                        _INT, ctypes.c_uint64, _VP, ctypes.c_uint, _PINT, _PINT]),
     "glq_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _INT]),
     "glq_plan": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _INT,
                         _PINT, _PINT]),

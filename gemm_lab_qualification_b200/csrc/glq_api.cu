@@ -87,6 +87,48 @@ int validate(int dtype, int epilogue, int64_t m, int64_t n, int64_t k, int split
   return GLQ_OK;
 }
 
+// Static scratch of glq_linear_gather_static: the fused gather's arrival
+// counters, one word per slot, for callers that cannot allocate.  Host code
+// must not use this name as a device address; static_gather_scratch() looks
+// the address up once per device.
+static __device__ __align__(256) unsigned int g_static_gather_scratch[GLQ_STATIC_GATHER_SLOTS];
+
+struct StaticScratchState {
+  std::once_flag once;
+  int status = GLQ_OK;
+  unsigned int* ptr = nullptr;
+};
+
+StaticScratchState g_static_scratch[kMaxDevices];
+
+// Device address of g_static_gather_scratch on the current device, zeroed
+// once (first call per device, with that device current).
+int static_gather_scratch(unsigned int** out) {
+  DeviceState* dev_state = nullptr;
+  const int v = device_state(&dev_state);
+  if (v != GLQ_OK) return v;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_DEVICE;
+  }
+  StaticScratchState& st = g_static_scratch[dev];
+  std::call_once(st.once, [&st] {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_gather_scratch) != cudaSuccess ||
+        cudaMemset(ptr, 0, sizeof(g_static_gather_scratch)) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+      cudaGetLastError();
+      st.status = GLQ_ERR_CUDA;
+      return;
+    }
+    st.ptr = static_cast<unsigned int*>(ptr);
+    st.status = GLQ_OK;
+  });
+  *out = st.ptr;
+  return st.status;
+}
+
 }  // namespace
 
 int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
@@ -340,6 +382,30 @@ int glq_linear_gather(int dtype, const void* A, int64_t a_row_stride, int64_t a_
   return GLQ_OK;
 }
 
+int glq_linear_gather_static(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride,
+                             const void* B, int64_t b_k_stride, int64_t b_n_stride, const void* bias,
+                             int epilogue, void* const* y_ranks, int64_t y_row_stride, int64_t y_col_offset,
+                             int64_t M, int64_t N, int64_t K, int split_k, int rank, int world,
+                             uint64_t* const* signal_ranks, int counter_slot, uint64_t epoch, void* stream,
+                             unsigned int flags, int* path_out, int* split_out) {
+  if (path_out) *path_out = GLQ_PATH_EMPTY;
+  if (split_out) *split_out = 1;
+  if (counter_slot < 0 || counter_slot >= GLQ_STATIC_GATHER_SLOTS) return GLQ_ERR_SCRATCH;
+  unsigned int* scratch = nullptr;
+  const int v = glq::static_gather_scratch(&scratch);
+  if (v != GLQ_OK) return v;
+  unsigned int* counter = scratch + counter_slot;
+  // The kernel leaves the counter at zero, but a call whose wait expired may
+  // not have: start every call from zero, in stream order.
+  if (cudaMemsetAsync(counter, 0, sizeof(unsigned int), static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_CUDA;
+  }
+  return glq_linear_gather(dtype, A, a_row_stride, a_col_stride, B, b_k_stride, b_n_stride, bias, epilogue,
+                           y_ranks, y_row_stride, y_col_offset, M, N, K, split_k, rank, world, signal_ranks,
+                           counter, epoch, stream, flags, path_out, split_out);
+}
+
 int glq_linear_f16(const void* A, int64_t lda, int64_t a_col_stride, const void* B,
                    int64_t b_row_stride, int64_t b_col_stride, const void* bias, void* Y, int64_t ldy,
                    int M, int N, int K, int split_k, void* workspace, size_t workspace_bytes,
@@ -415,6 +481,7 @@ const char* glq_status_string(int status) {
     case GLQ_ERR_CUDA: return "CUDA runtime or driver call failed";
     case GLQ_ERR_DEVICE: return "no usable device: the kernels need a compute capability 10.0 (sm_100a) GPU";
     case GLQ_ERR_DEVICE_TIMEOUT: return "an in-kernel bounded wait expired";
+    case GLQ_ERR_SCRATCH: return "counter_slot outside the library's static scratch (0..GLQ_STATIC_GATHER_SLOTS-1)";
     default: return "unknown status";
   }
 }

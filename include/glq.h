@@ -12,7 +12,8 @@
  * (b_k_stride = N, b_n_stride = 1) is accepted through the same entry point.
  *
  * Every entry point is stateless apart from a per-device one-time set-up
- * (kernel attributes, the TMA encoder entry point), thread-safe, stream-ordered
+ * (kernel attributes, the TMA encoder entry point) and the shared counter
+ * array of glq_linear_gather_static, thread-safe, stream-ordered
  * on the caller's stream, never allocates device memory and never throws
  * across the boundary: each returns a glq_status.  All pointers are device
  * pointers unless stated otherwise.  `stream` is a cudaStream_t (NULL is the
@@ -85,7 +86,9 @@ enum glq_status {
   GLQ_ERR_CUDA = 6,             /* CUDA runtime or driver call failed */
   GLQ_ERR_DEVICE = 7,           /* no device, or not a compute 10.0 GPU */
   GLQ_ERR_DEVICE_TIMEOUT = 8,   /* an in-kernel bounded wait expired */
-  GLQ_STATUS_COUNT = 9
+  GLQ_ERR_SCRATCH = 9,          /* request beyond the static scratch of
+                                   glq_linear_gather_static */
+  GLQ_STATUS_COUNT = 10
 };
 
 #define GLQ_MAX_SPLIT 8
@@ -246,6 +249,46 @@ int glq_linear_gather(int dtype,
                       int rank, int world,
                       uint64_t* const* signal_ranks, unsigned int* counter, uint64_t epoch,
                       void* stream, unsigned int flags, int* path_out, int* split_out);
+
+/* Arrival-counter slots in the static scratch of glq_linear_gather_static
+ * (one 32-bit word each: 256 bytes per GPU that loads the library). */
+#define GLQ_STATIC_GATHER_SLOTS 64
+
+/*
+ * glq_linear_gather_static -- glq_linear_gather for callers that cannot
+ * allocate device memory.  The fused gather needs one private, zeroed 32-bit
+ * arrival counter per rank besides its inputs and outputs; some callers have
+ * no way to get one: a plugin or foreign-language host that only receives
+ * device pointers from its framework (the weights, the activations and the
+ * communicator's peer-mapped output and signal buffers) and owns no
+ * allocator, or a pipeline that must not call cudaMalloc because that
+ * synchronises the device.  This entry point takes the counter from a
+ * fixed array compiled into the library instead: GLQ_STATIC_GATHER_SLOTS
+ * words, held by every GPU that loads the library until the process exits.
+ * `counter_slot` picks the word; a slot outside 0..GLQ_STATIC_GATHER_SLOTS-1
+ * is rejected with GLQ_ERR_SCRATCH.  Every other argument and the result are
+ * those of glq_linear_gather (the caller still passes the inputs, the
+ * outputs and the signal slots), and nothing is allocated.
+ *
+ * The slot is cleared on the caller's stream before each launch.  All calls
+ * share the array: calls that use the same slot and overlap on the GPU
+ * (different streams, or several layers in flight) race and corrupt each
+ * other's completion; give such calls different slots.  The first call on a
+ * device looks up the array's device address and zeroes it once; make that
+ * first call before any stream capture.
+ *
+ * No counterpart in the reference (it has no multi-GPU path and no
+ * allocation-free entry points).
+ */
+int glq_linear_gather_static(int dtype,
+                             const void* A, int64_t a_row_stride, int64_t a_col_stride,
+                             const void* B, int64_t b_k_stride, int64_t b_n_stride,
+                             const void* bias, int epilogue,
+                             void* const* y_ranks, int64_t y_row_stride, int64_t y_col_offset,
+                             int64_t M, int64_t N, int64_t K, int split_k,
+                             int rank, int world,
+                             uint64_t* const* signal_ranks, int counter_slot, uint64_t epoch,
+                             void* stream, unsigned int flags, int* path_out, int* split_out);
 
 /* Names of paths and statuses (static strings, never NULL). */
 const char* glq_path_name(int path);

@@ -262,3 +262,23 @@ def test_gather_argument_validation():
     # valid arguments reach the device check: no sm_100a GPU here
     if not torch.cuda.is_available():
         assert gather_status() == 7
+
+
+def test_gather_static_rejects_slots_outside_the_scratch():
+    """The allocation-free gather takes its counter from a fixed array of
+    GLQ_STATIC_GATHER_SLOTS words; other slots are refused before any device work."""
+    lib = native.library()
+    VP = ctypes.c_void_p
+    ys = (VP * 1)(16)
+    sigs = (VP * 1)(16)
+
+    def call(slot):
+        return lib.glq_linear_gather_static(0, 16, 4096, 1, 16, 1, 4096, 16, 2, ys, 4096, 0, 32, 4096, 4096, 0,
+                                            0, 1, sigs, slot, 1, None, 0, None, None)
+    scratch = native.STATUS_NAMES.index("scratch")
+    assert call(-1) == scratch
+    assert call(native.STATIC_GATHER_SLOTS) == scratch
+    assert "static scratch" in native.status_string(scratch)
+    if not torch.cuda.is_available():
+        assert call(0) == 7
+        assert call(native.STATIC_GATHER_SLOTS - 1) == 7
