@@ -196,6 +196,13 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   // Split-K tiles hold at most 128 tokens (the merge buffers must fit in the
   // drained pipeline memory).
   if (c->split > 1 && c->tile_t > 128) c->tile_t = 128;
+  // Prefill-sized problems (256-token tiles, no split) with at least one
+  // wave of 256 x 256 output tiles: two M = 128 MMAs per K step share the
+  // token tile, doubling the FLOPs per staged byte.
+  if (c->split == 1 && c->tile_t == 256 &&
+      ((p.n + 255) / 256) * ((p.m + 255) / 256) >= static_cast<int64_t>(sms)) {
+    c->tile_n = 256;
+  }
   if (p.n % 128 != 0 || p.k % 64 != 0) {
     c->path = GLQ_PATH_TAIL;
   } else if (c->w_mn) {

@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int split = args.split;
   const int s = blockIdx.x;  // split index == CTA rank in the (split,1,1) cluster
-  const int tile_n = blockIdx.y;
-  const int tile_t = blockIdx.z;
+  // Token tiles vary fastest in launch order, so the CTAs resident at one
+  // time share W tiles (read from HBM once) and re-read the smaller A from L2.
+  const int tile_t = blockIdx.y;
+  const int tile_n = blockIdx.z;
   const int kb_begin = static_cast<int>((static_cast<long long>(s) * args.num_kb) / split);
   const int kb_end = static_cast<int>((static_cast<long long>(s + 1) * args.num_kb) / split);
   const int nkb = kb_end - kb_begin;
@@ -661,6 +663,7 @@ cudaError_t set_attrs_all() {
   cudaError_t e;
   if ((e = set_attrs<T, 16, 256, 4>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 32, 256, 4>()) != cudaSuccess) return e;
+  if ((e = set_attrs<T, 256, 256, 3>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 16, 128, kPairStages>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 32, 128, kPairStages>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 16, 128, 8>()) != cudaSuccess) return e;
@@ -757,8 +760,8 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   if (smem_bytes > budget) return cudaErrorInvalidValue;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>((p.n + TN - 1) / TN),
-                     static_cast<unsigned>((p.m + BT - 1) / BT));
+  cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>((p.m + BT - 1) / BT),
+                     static_cast<unsigned>((p.n + TN - 1) / TN));
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
@@ -781,6 +784,7 @@ cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int s
     switch (tile_t) {
       case 16: return launch_typed<T, 16, 256, 4, WMN, GATHER>(p, split, g, err, s);
       case 32: return launch_typed<T, 32, 256, 4, WMN, GATHER>(p, split, g, err, s);
+      case 256: return launch_typed<T, 256, 256, 3, WMN, GATHER>(p, split, g, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
