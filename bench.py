@@ -73,6 +73,8 @@ def parse_args(argv=None):
     p.add_argument("--inner", type=int, default=10, help="back-to-back calls per timed sample")
     p.add_argument("--sweep", type=str, default=",".join(map(str, SWEEP_M)),
                    help="comma-separated M values of the step (default 1,8,32,128)")
+    p.add_argument("--no-sharded-shapes", action="store_true",
+                   help="N > 1: skip the BASELINE sharded shapes (N = 8192 / 28672, K = 8192)")
     return p.parse_args(argv)
 
 
@@ -551,6 +553,84 @@ def multi_gpu(args, torch, dist, dev, world: int, rank: int) -> dict:
             "h2d": ha.numel() * 2 + hw.numel() * 2 + hb.numel() * 2, "d2h": hy.numel() * 2}
 
 
+SHARDED_SHAPES = ((8192, 8192), (28672, 8192))  # (N, K) of BASELINE's column-parallel configs
+SHARDED_M = (1, 32, 128, 4096)
+
+
+def sharded_shapes(args, torch, dist, dev, world: int, rank: int) -> list[dict]:
+    """BASELINE's column-parallel shapes, strong scaling: W [N, K] split along N
+    over the ranks, fused bias+SiLU, all-gather fused into the kernel.  Inputs
+    are uniform [-0.5, 0.5) draws of the device generator seeded 7 (the full
+    layer is generated identically on every rank and sliced).  Rank 0 also
+    times the unsharded layer alone on its GPU for the same shape."""
+    from gemm_lab_qualification_b200 import _native, sharded
+    from gemm_lab_qualification_b200.evidence import device_measure
+    peaks = {}
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    tensor_peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    out = []
+    for n_total, k in SHARDED_SHAPES:
+        gen = torch.Generator(device=dev).manual_seed(7)
+        w = (torch.rand((n_total, k), generator=gen, device=dev, dtype=torch.float32) - 0.5).half()
+        bias = (torch.rand((n_total,), generator=gen, device=dev, dtype=torch.float32) - 0.5).half()
+        for m in SHARDED_M:
+            a = (torch.rand((m, k), generator=gen, device=dev, dtype=torch.float32) - 0.5).half()
+            layer = sharded.ColumnParallelLinear(w, bias, "silu", device=dev, fused_gather=True, max_rows=m)
+            ns = layer.weight.shape[0]
+            y = layer(a)
+            torch.cuda.synchronize()
+            # gate: this rank's view of every slice against a torch FP32 reference (sampled rows for large M)
+            rows = torch.arange(0, m, max(1, m // 64), device=dev)
+            ref = torch.nn.functional.silu(a[rows].float() @ w.float().t() + bias.float())
+            err = (y[rows].float() - ref).abs()
+            if not bool((err <= 0.02 + 0.002 * ref.abs()).all()):
+                raise SystemExit(f"rank {rank}: sharded shape N={n_total} M={m} failed the gate")
+            inner = 3 if m >= 1024 else args.inner
+            rounds = max(5, min(args.steps, 20))
+            call = lambda: layer.gather(a, layer.weight.t(), layer.bias, _native.EPILOGUE_BIAS_SILU)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(inner):
+                call()
+            host_us = (time.perf_counter() - t0) * 1e6 / inner
+            torch.cuda.synchronize()
+            hold = max(400.0, 3.0 * inner * host_us)
+            device_measure({"x": call}, rounds=2, inner=inner, hold_us=hold)
+            dist.barrier()
+            raw = device_measure({"x": call}, rounds=rounds, inner=inner, hold_us=hold)["x"]
+            dist.barrier()
+            t = torch.tensor([statistics.median(raw)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t[0]) * 1e3
+            single_us = None
+            if rank == 0:
+                y1 = torch.empty((m, n_total), dtype=torch.float16, device=dev)
+                one = lambda: _native.linear(a, w.t(), y1, bias, _native.EPILOGUE_BIAS_SILU)
+                device_measure({"x": one}, rounds=2, inner=inner, hold_us=hold)
+                single_us = statistics.median(device_measure({"x": one}, rounds=rounds, inner=inner,
+                                                             hold_us=hold)["x"]) * 1e3
+                del y1
+            dist.barrier()
+            flops = 2 * m * n_total * k
+            rank_bytes = 2 * (m * k + ns * k + m * n_total) + 2 * ns
+            row = {"n": n_total, "k": k, "m": m, "n_per_rank": ns, "p50_us": us,
+                   "tflops_total": flops / (us * 1e-6) / 1e12,
+                   "tensor_frac_per_rank": flops / world / (us * 1e-6) / 1e12 / tensor_peak,
+                   "hbm_gbs_per_rank": rank_bytes / (us * 1e-6) / 1e9,
+                   "nvlink_bytes_per_rank": 2 * m * ns * (world - 1),
+                   "single_gpu_unsharded_us": single_us,
+                   "speedup_vs_single_gpu": (single_us / us) if single_us else None}
+            out.append(row)
+            del layer, y, a
+            torch.cuda.empty_cache()
+        del w, bias
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_native(args) -> int:
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -569,6 +649,8 @@ def run_native(args) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         try:
             res = multi_gpu(args, torch, dist, dev, world, rank)
+            if not args.no_sharded_shapes:
+                res["sharded_shapes"] = sharded_shapes(args, torch, dist, dev, world, rank)
         finally:
             dist.barrier()
             dist.destroy_process_group()
@@ -603,6 +685,13 @@ def run_native(args) -> int:
                                  "note": "per-rank HBM bytes (A, W slice, bias, gathered Y) over the mean layer "
                                          "call; the NVLink leg (this rank's slice to every peer) is the smaller "
                                          "bound at these sizes"}}
+            if "sharded_shapes" in res:
+                line["sharded_shapes"] = {
+                    "workload": "BASELINE column-parallel configs: fused linear+bias+SiLU, W [N, K] split along N "
+                                "over the ranks (strong scaling), all-gather fused into the kernel; device-"
+                                "generator seed-7 uniform inputs; p50 of back-to-back calls, max over ranks; "
+                                "tensor_frac against bf16_tflops_sustained of MEASURED_PEAKS.json",
+                    "rows": res["sharded_shapes"]}
             print(json.dumps(line), flush=True)
         return 0
 
