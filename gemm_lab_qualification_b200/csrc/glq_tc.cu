@@ -565,8 +565,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // resets the counter, fences at system scope (so every CTA's stores
   // precede, in causality order, what follows), writes the epoch into this
   // rank's slot of every rank's signal array and waits, bounded, until every
-  // rank has written its slot here, reading the slots with system-scope
-  // acquire loads (which order the peers' slices before the kernel's end).
+  // rank has written its slot here, one lane per rank reading the slots with
+  // system-scope acquire loads (which order the peers' slices before the
+  // kernel's end).
   // Only CTA 0 pays a system-scope fence: hundreds of concurrent ones
   // serialise.  The kernel therefore completes only when this rank's output
   // holds all slices.  Every wait is bounded; on expiry the device error
@@ -576,14 +577,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
       ptx::fence_acq_rel_gpu();
       ptx::red_add_relaxed_gpu(args.counter, 1u);
-      if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
-        const uint64_t t0 = ptx::globaltimer_ns();
-        bool ok = true;
-        uint32_t polls = 0;
-        auto expired = [&]() {
-          return (++polls & 63u) == 0u && (ptx::globaltimer_ns() - t0 > kWaitBudgetNs || polls > (1u << 26));
-        };
+    }
+    if (warp == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+      const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+      const uint64_t t0 = ptx::globaltimer_ns();
+      uint32_t polls = 0;
+      auto expired = [&]() {
+        return (++polls & 63u) == 0u && (ptx::globaltimer_ns() - t0 > kWaitBudgetNs || polls > (1u << 26));
+      };
+      bool ok = true;
+      if (lane == 0) {
         while (ptx::ld_relaxed_gpu_u32(args.counter) < total) {
           if (expired()) {
             ok = false;
@@ -594,17 +597,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           *args.counter = 0u;  // every CTA of this grid has counted in
           ptx::fence_acq_rel_sys();
           for (int r = 0; r < args.n_out; ++r) ptx::st_relaxed_sys_u64(args.sig_out[r] + args.rank, args.epoch);
-          for (int r = 0; r < args.n_out && ok; ++r) {
-            while (ptx::ld_acquire_sys_u64(args.sig_in + r) < args.epoch) {
-              if (expired()) {
-                ok = false;
-                break;
-              }
-            }
+        }
+      }
+      // Lane r waits for rank r's epoch (all ranks' slots polled at once).
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (ok && lane < args.n_out) {
+        while (ptx::ld_acquire_sys_u64(args.sig_in + lane) < args.epoch) {
+          if (expired()) {
+            ok = false;
+            break;
           }
         }
-        if (!ok) atomicOr(args.err, kErrTimeoutPeer);
       }
+      const bool all_ok = __all_sync(0xffffffffu, ok);
+      if (lane == 0 && !all_ok) atomicOr(args.err, kErrTimeoutPeer);
     }
   }
 }
