@@ -102,10 +102,49 @@ def build_bench(force: bool = False) -> Path | None:
     return BENCH_BINARY
 
 
+def torch_binding_path() -> Path:
+    import sysconfig
+    return PACKAGE_DIR / ("_glq_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_torch_binding(force: bool = False) -> Path:
+    """Build _glq_torch (csrc/glq_torch.cpp): the operator API's checks and
+    launch in one native call, linked against libglq.so and torch."""
+    import sysconfig
+
+    import torch
+    import torch.utils.cpp_extension as cpp_ext
+
+    src = CSRC / "glq_torch.cpp"
+    out = torch_binding_path()
+    lib = build_library(force=force)
+    if not (force or _stale(out, [src, lib, *_headers()])):
+        return out
+    try:
+        includes = cpp_ext.include_paths(device_type="cuda")
+    except TypeError:
+        includes = cpp_ext.include_paths(cuda=True)
+    includes = [*includes, sysconfig.get_paths()["include"], str(INCLUDE)]
+    torch_lib = cpp_ext.library_paths()[0]
+    tmp = out.with_suffix(".tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           "-DTORCH_EXTENSION_NAME=_glq_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *cpp_ext._get_pybind11_abi_build_flags(), *[f"-I{p}" for p in includes], str(src), "-o", str(tmp),
+           f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           f"-L{PACKAGE_DIR}", "-lglq", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"_glq_torch build failed:\n{proc.stderr}")
+    os.replace(tmp, out)
+    return out
+
+
 def main(argv: list[str]) -> int:
     force = "--force" in argv
     verbose = "-v" in argv or "--verbose" in argv
     print(build_library(force=force, verbose=verbose))
+    print(build_torch_binding(force=force))
     bench = build_bench(force=force)
     if bench is not None:
         print(bench)

@@ -78,6 +78,33 @@ def _record(result: tuple[str, int]) -> None:
     _last.value = result
 
 
+_ext = None
+
+
+def _binding():
+    """The native call path (csrc/glq_torch.cpp): argument checks with the
+    messages below plus the glq_linear_ex launch, in one C++ call."""
+    global _ext
+    if _ext is None:
+        _native.library()  # fails loudly when libglq.so is missing
+        try:
+            from . import _glq_torch
+        except ImportError as exc:
+            raise _native.NativeLibraryMissing(
+                "the _glq_torch binding is not built; build it with "
+                "`python -m gemm_lab_qualification_b200.build`") from exc
+        _ext = _glq_torch
+    return _ext
+
+
+def _launch(op: str, a: torch.Tensor, b: torch.Tensor, output: torch.Tensor, bias: torch.Tensor | None = None,
+            epilogue: int = _native.EPILOGUE_NONE, split_k: int = 0, partial: torch.Tensor | None = None) -> None:
+    status, path, split = _binding().linear(op, a, b, output, bias, epilogue, split_k, partial, _flags())
+    if status != _native.STATUS_OK:
+        raise _native.GlqError(status, "glq_linear_ex")
+    _last.value = (_native.PATHS[path], split)
+
+
 def _validate_inputs(a: torch.Tensor, b: torch.Tensor, operation: str) -> tuple[int, int, int]:
     """Contract checks of kernels.py:132-145, minus the contiguity rule."""
     if a.ndim != 2 or b.ndim != 2:
@@ -116,13 +143,9 @@ def linear_into(a: torch.Tensor, b: torch.Tensor, output: torch.Tensor, bias: to
         raise ValueError("activation must be None or 'silu'")
     if activation == "silu" and bias is None:
         raise ValueError("the fused SiLU epilogue takes a bias")
-    m, n, _ = _validate_inputs(a, b, "linear")
-    _validate_output(output, a, m, n)
-    if bias is not None:
-        _validate_bias(bias, a, n)
     epilogue = (_native.EPILOGUE_NONE if bias is None else
                 _native.EPILOGUE_BIAS_SILU if activation == "silu" else _native.EPILOGUE_BIAS)
-    _record(_native.linear(a, b, output, bias, epilogue, split_k, partial, flags=_flags()))
+    _launch("linear", a, b, output, bias, epilogue, split_k, partial)
     return output
 
 
@@ -137,9 +160,7 @@ def planned_path(a: torch.Tensor, b: torch.Tensor, split_k: int = 0) -> tuple[st
 # ---------------------------------------------------------------- GEMM (kernels.py:148-188)
 
 def triton_matmul_into(a: torch.Tensor, b: torch.Tensor, output: torch.Tensor) -> torch.Tensor:
-    m, n, _ = _validate_inputs(a, b, "triton_matmul")
-    _validate_output(output, a, m, n)
-    _record(_native.linear(a, b, output, flags=_flags()))
+    _launch("triton_matmul", a, b, output)
     return output
 
 
@@ -164,10 +185,7 @@ class TritonMatmulPlan:
 
 def triton_bias_silu_into(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor,
                           output: torch.Tensor) -> torch.Tensor:
-    m, n, _ = _validate_inputs(a, b, "triton_bias_silu")
-    _validate_bias(bias, a, n)
-    _validate_output(output, a, m, n)
-    _record(_native.linear(a, b, output, bias, _native.EPILOGUE_BIAS_SILU, flags=_flags()))
+    _launch("triton_bias_silu", a, b, output, bias, _native.EPILOGUE_BIAS_SILU)
     return output
 
 
@@ -217,8 +235,7 @@ def triton_splitk_matmul_into(a: torch.Tensor, b: torch.Tensor, partial: torch.T
         raise ValueError("partial tensor has the wrong shape, device, or dtype")
     if not partial.is_contiguous():
         raise ValueError("partial tensor must be contiguous")
-    _validate_output(output, a, m, n)
-    _record(_native.linear(a, b, output, None, _native.EPILOGUE_NONE, split_k, partial, flags=_flags()))
+    _launch("triton_splitk_matmul", a, b, output, None, _native.EPILOGUE_NONE, split_k, partial)
     return output
 
 

@@ -158,7 +158,9 @@ class FusedGather:
             raise ValueError("dtype differs from the gather buffers")
         self.epoch += 1
         parity = self.epoch & 1
-        _native.linear_gather(a, b, bias, epilogue, self._y_ptrs[parity], self.n_total, self.rank * n_local,
-                              self.rank, self._sig_ptrs, self._counter, self.epoch, split_k=split_k,
-                              flags=kernels._flags())
+        status, _, _ = kernels._binding().linear_gather(a, b, bias, epilogue, self._y_ptrs[parity], self.n_total,
+                                                        self.rank * n_local, self.rank, self._sig_ptrs,
+                                                        self._counter, self.epoch, split_k, kernels._flags())
+        if status != _native.STATUS_OK:
+            raise _native.GlqError(status, "glq_linear_gather")
         return self.output(parity, m)
