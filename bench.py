@@ -325,6 +325,22 @@ def single_gpu(args, torch, dev) -> dict:
     cublas = device_measure({f"{v}/m{m}": vendor(m, v) for m in sweep_m for v in ("fused", "plain")},
                             rounds=max(10, args.steps // 3), inner=args.inner)
 
+    # The lab harness's own protocol (evidence.torch_measure: no GPU hold, so
+    # host dispatch is inside the span; the same resident W every call, warm
+    # L2; 20 warm-ups, 31 randomised samples of 10 calls): what
+    # qualification.benchmark() would report for the drop-in operators.
+    from gemm_lab_qualification_b200.evidence import torch_measure
+    lab = {}
+    for m in sweep_m:
+        st = state[m]
+        w0 = st["w"][0]
+        res = torch_measure({
+            "ours": lambda st=st, w0=w0: kernels.triton_bias_silu_into(st["a"], w0.t(), st["bias"], st["fused"]),
+            "torch": lambda st=st, w0=w0: torch.nn.functional.silu(
+                torch.nn.functional.linear(st["a"], w0, st["bias"]), inplace=True),
+        }, samples=31, warmup=20, inner=args.inner)
+        lab[m] = {k: v["cuda_event"]["p50_ms"] * 1e3 for k, v in res["measurements"].items()}
+
     # The fused call on the lab's own B = [K, N] operand (MN-major W tiles).
     def b_kn(m):
         st = state[m]
@@ -374,6 +390,8 @@ def single_gpu(args, torch, dev) -> dict:
         for v in ("fused", "plain"):
             row[f"cublas_{v}_p50_us"] = statistics.median(cublas[f"{v}/m{m}"]) * 1e3
         row["fused_b_kn_p50_us"] = statistics.median(kn[f"fused/m{m}"]) * 1e3
+        row["fused_lab_protocol_p50_us"] = lab[m]["ours"]
+        row["torch_fragment_lab_protocol_p50_us"] = lab[m]["torch"]
         row["b_kn_path"] = paths[f"kn{m}"][0]
         sweep[str(m)] = row
 

@@ -55,7 +55,7 @@ int device_state(DeviceState** out) {
     st.sm_count = sms > 0 ? sms : 148;
     void* word = nullptr;
     if (cudaGetSymbolAddress(&word, g_device_error_word) != cudaSuccess ||
-        tc_prepare_device() != cudaSuccess) {
+        tc_prepare_device() != cudaSuccess || gemv_prepare_device() != cudaSuccess) {
       cudaGetLastError();
       st.status = GLQ_ERR_CUDA;
       return;
@@ -172,7 +172,12 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   }
   c->w_mn = w_mnmajor ? 1 : 0;
   if (p.m == 1 && w_kmajor && !p.require_tc) {
-    c->kernel = kKernelGemv;
+    const int sms = sm_count > 0 ? sm_count : 148;
+    // The ring GEMV holds a whole SM per CTA, so with static weights (where a
+    // call's weight stream should start while its predecessor drains) the
+    // register GEMV, whose blocks can be resident early, is faster.
+    const bool ring = split_k <= 1 && (p.flags & GLQ_FLAG_STATIC_WEIGHTS) == 0 && gemv_ring_fits(p.n, p.k, sms);
+    c->kernel = ring ? kKernelGemvRing : kKernelGemv;
     c->split = split_k > 0 ? split_k : 1;
     c->path = (p.k % 8 != 0) ? GLQ_PATH_TAIL : GLQ_PATH_GEMV_M1;
     return GLQ_OK;
@@ -307,6 +312,7 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
     case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
+    case glq::kKernelGemvRing: e = glq::launch_gemv_ring(p, dev->error_word, s, dev->sm_count); break;
     case glq::kKernelTc:
       e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, nullptr, dev->error_word, s);
       break;

@@ -71,6 +71,7 @@ enum Kernel : int {
   kKernelGemv = 2,
   kKernelTc = 3,
   kKernelGeneric = 4,
+  kKernelGemvRing = 5,  // M = 1 GEMV fed by the TMA engine (path gemv_m1)
 };
 
 // Pure host planning (glq_plan and glq_linear share it).
@@ -108,6 +109,22 @@ inline int tc_token_tile(int64_t m) {
 // Launchers (return cudaError_t of the launch).  err = device error word.
 cudaError_t launch_fill(const Problem& p, cudaStream_t s);
 cudaError_t launch_gemv(const Problem& p, int split, unsigned int* err, cudaStream_t s);
+cudaError_t launch_gemv_ring(const Problem& p, unsigned int* err, cudaStream_t s, int sm_count);
+
+// Where the ring GEMV runs: rows of at most 8 KB (K <= 4096, K % 8 == 0)
+// and at most 32 rows per SM, i.e. layers the register GEMV covers in one
+// wave, so the whole weight can be requested at once.  Taller layers stream
+// better through the register GEMV's successive waves (measured: 28672 x 8192
+// 73 us register GEMV vs 136 us ring), and the ring's shared memory (A, the
+// per-row partials and at least two stages) must fit in 227 KB.
+inline bool gemv_ring_fits(int64_t n, int64_t k, int sm_count) {
+  if (k % 8 != 0 || k <= 0 || k > 4096 || n <= 0) return false;
+  const int64_t ctas = n < sm_count ? n : sm_count;
+  const int64_t rows = (n + ctas - 1) / ctas;
+  if (rows > 32) return false;
+  const int64_t fixed = 2 * k + ((rows * 4 + 15) / 16) * 16 + 1024;
+  return fixed + 2 * k * 2 <= 232448;
+}
 cudaError_t launch_generic(const Problem& p, cudaStream_t s);
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
@@ -117,5 +134,7 @@ cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int s
 
 // Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).
 cudaError_t tc_prepare_device();
+// ... and of the ring GEMV.
+cudaError_t gemv_prepare_device();
 
 }  // namespace glq

@@ -39,6 +39,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// Plain arrive (count 1), release at CTA scope: this thread's earlier reads
+// of the guarded buffer are done.
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
@@ -128,6 +134,17 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+
+// 1-D bulk copy (TMA engine) of `bytes` from global memory into this CTA's
+// shared memory, completing `bar`'s transaction count.  Both addresses
+// 16-byte aligned, size a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
