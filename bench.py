@@ -398,7 +398,7 @@ def single_gpu(args, torch, dev) -> dict:
     head = sweep[str(args.m)]
     mean_s = head["fused_mean_us"] * 1e-6
     achieved = head["bytes_fused"] / mean_s / 1e9
-    kernel_tag = "gemv" if args.m == 1 else "tc_linear"
+    kernel_tag = "gemv" if args.m == 1 else "tc_linear"  # profiles/*.md tags (gemv_m1: the ring GEMV)
     traffic = profiled_traffic(f"{kernel_tag}_m{args.m}")
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": traffic, "peak_source": peak_src,
