@@ -367,6 +367,37 @@ def single_gpu(args, torch, dev) -> dict:
         warm.update(device_measure({key: call(m_key, v_key, rotate=False)}, rounds=max(5, args.steps // 10),
                                    inner=args.inner))
 
+    # The MLP shapes gated by the lab's adaptive_bias_silu_path (4096 <-> 11008,
+    # kernels.py:295): fused call vs the cuBLASLt fragment, rotating weights.
+    mlp = []
+    for n_m, k_m in ((11008, 4096), (4096, 11008)):
+        w_bytes_m = n_m * k_m * 2
+        copies_m = max(4, math.ceil(3 * l2 / w_bytes_m))
+        for m in (1, 32):
+            a_m, w_m, b_m = workloads.uniform_inputs(m, n_m, k_m)
+            da_m, db_m = a_m.to(dev), b_m.to(dev)
+            ws_m = [w_m.to(dev) for _ in range(copies_m)]
+            y_m = torch.empty((m, n_m), dtype=torch.float16, device=dev)
+            cnt = {"i": 0}
+
+            def ours(da_m=da_m, db_m=db_m, ws_m=ws_m, y_m=y_m, cnt=cnt, copies_m=copies_m):
+                cnt["i"] += 1
+                kernels.triton_bias_silu_into(da_m, ws_m[cnt["i"] % copies_m].t(), db_m, y_m)
+
+            def theirs(da_m=da_m, db_m=db_m, ws_m=ws_m, cnt=cnt, copies_m=copies_m):
+                cnt["i"] += 1
+                torch.nn.functional.silu(torch.nn.functional.linear(da_m, ws_m[cnt["i"] % copies_m], db_m),
+                                         inplace=True)
+            ours()
+            path_m = kernels.last_path()
+            fns_m = {"ours": ours, "cublas": theirs}
+            device_measure(fns_m, rounds=3, inner=args.inner)
+            raw_m = device_measure(fns_m, rounds=max(10, args.steps // 5), inner=args.inner)
+            us = statistics.median(raw_m["ours"]) * 1e3
+            mlp.append({"m": m, "n": n_m, "k": k_m, "path": list(path_m), "fused_p50_us": us,
+                        "cublas_fused_p50_us": statistics.median(raw_m["cublas"]) * 1e3,
+                        "gbs": 2 * (m * k_m + n_m * k_m + m * n_m + n_m) / (us * 1e-6) / 1e9})
+            del ws_m
     peak, peak_src = measured_hbm_peak()
     sweep = {}
     for m in sweep_m:
@@ -405,7 +436,8 @@ def single_gpu(args, torch, dev) -> dict:
                 "kernel": f"{kernel_tag} (fused, M={args.m}, path {head['path']}, split {head['split']})",
                 "algorithmic_bytes_per_launch": head["bytes_fused"], "launch_mean_us": head["fused_mean_us"]}
     ms_per_step = sum(statistics.fmean(v) for v in raw.values()) * args.inner
-    return {"value": head["fused_p50_us"], "ms_per_step": ms_per_step, "sweep": sweep, "roofline": roofline,
+    return {"value": head["fused_p50_us"], "ms_per_step": ms_per_step, "sweep": sweep, "mlp_shapes": mlp,
+            "roofline": roofline,
             "clocks": clocks.summary(), "copies": copies, "l2_bytes": l2, "wall_s": wall,
             "gpu_launches": args.steps * len(fns) * args.inner, "state": state}
 
@@ -726,7 +758,7 @@ def run_native(args) -> int:
                        "l2": f"inputs larger than L2: {res['copies']} rotating W copies "
                              f"({res['copies'] * 32} MiB) > L2 {res['l2_bytes'] / 2**20:.0f} MiB"},
             "impl": "native", "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
-            "clocks": res["clocks"], "sweep": res["sweep"]}
+            "clocks": res["clocks"], "sweep": res["sweep"], "mlp_shapes": res["mlp_shapes"]}
     if not args.no_e2e:
         e2e = e2e_public_api(args, torch, dev, rounds=max(10, min(args.steps, 50)))
         line["e2e"] = e2e["all_inputs"]

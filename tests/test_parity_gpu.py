@@ -418,6 +418,21 @@ def test_wide_layer_256_row_tiles(cuda_device, m):
     oracle.compare(host(out), oracle.linear_reference(a, w[:8000], bias[:8000], silu=True), U_ATOL, U_RTOL)
 
 
+@pytest.mark.parametrize("m", [1, 32, 128, 512])
+@pytest.mark.parametrize("n,k", [(11008, 4096), (4096, 11008)])
+def test_mlp_shapes(cuda_device, m, n, k):
+    """The MLP shapes the lab's adaptive_bias_silu_path gates on (kernels.py:295,
+    4096 <-> 11008), both weight layouts, against the FP64 oracle."""
+    a, w, bias = workloads.uniform_inputs(m, n, k)
+    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    expected = oracle.linear_reference(a, w, bias, silu=True, samples=8)
+    out = kernels.adaptive_bias_silu(da, dw.t(), db)
+    oracle.compare(host(out), expected, U_ATOL, U_RTOL)
+    out_kn = kernels.triton_bias_silu(da, dw.t().contiguous(), db)
+    assert kernels.last_path()[0] == "tc_kn"
+    oracle.compare(host(out_kn), expected, U_ATOL, U_RTOL)
+
+
 def test_column_parallel_single_rank(cuda_device, tmp_path):
     """The sharded layer on a one-rank NCCL group equals the unsharded call."""
     import torch.distributed as dist
