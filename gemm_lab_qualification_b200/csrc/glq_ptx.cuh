@@ -147,6 +147,26 @@ __device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint
       : "memory");
 }
 
+// 1-D bulk copy (TMA engine) from this CTA's shared memory to global memory
+// (local or peer-mapped), tracked by the issuing thread's bulk async-group.
+// 16-byte aligned addresses, size a multiple of 16.
+__device__ __forceinline__ void bulk_store_1d(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(src), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until this thread's committed bulk copies have completed (written).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's async-proxy global accesses (completed bulk copies)
+// with its later generic-proxy ones.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, %1;" : "=l"(p) : "f"(1.0f));

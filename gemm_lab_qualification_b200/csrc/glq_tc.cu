@@ -144,6 +144,7 @@ struct TcArgs {
   unsigned long long epoch;
   int rank;
   uint32_t ys_offset;  // fused gather: FP16 output tile staging (bytes from the aligned base); ~0u = none
+  int bulk_out;        // fused gather: staged rows leave by bulk copies (N % 8 == 0)
   uint32_t recv_offset;     // split-K receive buffer, bytes from the 1024-aligned base
   uint32_t stage_offset;    // split-K send staging buffer (inside the drained pipeline)
   int recv_overlaps;        // 1: the receive buffer reuses the drained pipeline stages
@@ -370,12 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // NVLink-friendly store per 8 outputs instead of eight 2-byte ones).
   T* const y = static_cast<T*>(args.y_out[0]);
   const int out_first = GATHER ? static_cast<int>((blockIdx.y + blockIdx.z) % static_cast<unsigned>(args.n_out)) : 0;
-  const bool stage_out = GATHER && args.ys_offset != ~0u;
-  T* const ys = reinterpret_cast<T*>(smem + (stage_out ? args.ys_offset : 0u));
+  const bool gather_staged = GATHER && args.ys_offset != ~0u;
+  T* const ys = reinterpret_cast<T*>(smem + (gather_staged ? args.ys_offset : 0u));
   // mm: token within this CTA's token tile; mm_base: first token of the staged rows.
   auto store = [&](int mm, int mm_base, T v) {
     if constexpr (GATHER) {
-      if (stage_out) {
+      if (gather_staged) {
         ys[(mm - mm_base) * TN + n_local] = v;
       } else {
         store_out<T>(args, (m0 + mm) * args.ldy + n, v, out_first);
@@ -387,11 +388,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Staged rows [mm_base, mm_base + rows) of the tile to every output.
   auto flush_staged = [&](int mm_base, int rows) {
     if constexpr (GATHER) {
-      if (!stage_out) return;
+      if (!gather_staged) return;
+      const long long n_tile = static_cast<long long>(tile_n) * TN;
+      if (args.bulk_out) {
+        // One TMA-engine copy per (token row, rank): 256-byte NVLink writes
+        // instead of 16-byte stores from the SM.
+        ptx::fence_proxy_async_smem();
+        __syncthreads();
+        if (warp == 0) {
+          const long long valid = min(static_cast<long long>(TN), static_cast<long long>(args.n) - n_tile);
+          const uint32_t bytes = static_cast<uint32_t>(valid) * static_cast<uint32_t>(sizeof(T));
+          for (int idx = lane; valid > 0 && idx < rows * args.n_out; idx += 32) {
+            const int row = idx / args.n_out;
+            int o = out_first + (idx - row * args.n_out);
+            if (o >= args.n_out) o -= args.n_out;
+            ptx::bulk_store_1d(static_cast<T*>(args.y_out[o]) + (m0 + mm_base + row) * args.ldy + n_tile,
+                               ptx::smem_addr(ys + row * TN), bytes);
+          }
+          ptx::bulk_commit();
+          ptx::bulk_wait_all();
+          ptx::fence_proxy_async_global();
+        }
+        return;
+      }
       __syncthreads();
       constexpr int kVec = 8;                // FP16/BF16 outputs per 16-byte store
       constexpr int kChunks = TN / kVec;
-      const long long n_tile = static_cast<long long>(tile_n) * TN;
       for (int idx = threadIdx.x; idx < rows * kChunks; idx += kThreads) {
         const int row = idx / kChunks;
         const int c = idx - row * kChunks;
@@ -760,6 +782,8 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
     const uint32_t rows = split > 1 ? 4u * ((BT / 4 + split - 1) / split) : static_cast<uint32_t>(BT);
     if (bases_ok && ys_off + rows * TN * static_cast<uint32_t>(esz) <= Cfg::kPipeBytes) args.ys_offset = ys_off;
   }
+  // Bulk copies need 16-byte row segments: every tile's valid width a multiple of 8.
+  args.bulk_out = (args.ys_offset != ~0u && p.n % 8 == 0) ? 1 : 0;
   const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : Cfg::kPipeBytes;
   args.barrier_offset = (body + 15u) & ~15u;
   const uint32_t smem_bytes = 1024 + args.barrier_offset + Cfg::kBarrierBytes;
