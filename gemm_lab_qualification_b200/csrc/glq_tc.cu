@@ -16,12 +16,19 @@
 //     two warps per 32-lane TMEM quarter splitting the token columns.
 //   * Split-K: the K ranges of one tile are the CTAs of one thread-block
 //     cluster.  After the main loop every CTA stages its FP32 partial tile in
-//     its drained pipeline memory and ships each owner's 4-token groups with
-//     one DSMEM bulk copy that completes on the owner's receive mbarrier; the
-//     owner waits only on that barrier, sums the S partials of its groups in
-//     split order 0..S-1 from its own shared memory, applies bias + SiLU and
-//     stores.  The merge order is fixed, so results are bitwise
-//     reproducible, and the only spin-waits are bounded mbarrier waits.
+//     its drained pipeline memory; lanes of warp 0 ship each other owner's
+//     4-token groups with one DSMEM bulk copy each (rotated owner order),
+//     completing on the owner's receive mbarrier; the owner reads its own
+//     groups in place, waits only on that barrier, sums the S partials in
+//     split order 0..S-1, applies bias + SiLU and stores.  The merge order is
+//     fixed, so results are bitwise reproducible, and the only spin-waits are
+//     bounded mbarrier waits.
+//   * Prefill (M > 128): 256-token tiles launched token-tile-fastest (the
+//     resident CTAs share W tiles); 256 x 256 output tiles when they fill a
+//     wave.
+//   * GATHER: the column-parallel layer's all-gather runs in the epilogue
+//     (every rank's output over NVLink, then a bounded epoch handshake);
+//     see the completion block at the end of the kernel.
 //   * Programmatic dependent launch: every thread waits for the predecessor
 //     grid (griddepcontrol.wait) before touching global memory and then lets
 //     the next grid launch, so back-to-back calls overlap launch latency,
@@ -457,11 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // drained pipeline memory as [group][row] (16 bytes per entry, so
     // consecutive rows are consecutive: no bank conflicts).  4-token groups
     // are dealt to the S ranks as [r*G/S, (r+1)*G/S), so the groups of rank r
-    // form one contiguous block; thread 0 ships it to rank r's receive slot
-    // recv[src = this rank] with one bulk copy that completes its bytes on
-    // rank r's receive barrier.  Each owner waits only on that
-    // barrier, sums the S partials of its groups in split order 0..S-1 from
-    // its own shared memory, applies bias + SiLU and stores.
+    // form one contiguous block; lane (r - s) mod S of warp 0 ships it to
+    // rank r's receive slot for source s with one bulk copy that completes
+    // its bytes on rank r's receive barrier.  Each owner waits only on that
+    // barrier, then sums the S partials of its groups in split order 0..S-1
+    // (its own from its staging buffer), applies bias + SiLU and stores.
     const uint32_t recv = sbase + args.recv_offset;
     const uint32_t stage_out = sbase + args.stage_offset;
     if (!recv_dedicated) {
