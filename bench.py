@@ -106,18 +106,71 @@ def profiled_traffic(kernel_tag: str) -> int | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 100 ms (if present)."""
+    """SM clocks, power and clock-event reasons sampled DURING a timed region.
+
+    NVML (read-only queries) is polled from a thread every 10 ms, with one
+    sample taken on entry, so that even a region of a few milliseconds is
+    covered; without NVML, ``nvidia-smi -lms 100`` is the fallback.  The NVML
+    device is found by the CUDA device's UUID, so CUDA_VISIBLE_DEVICES
+    renumbering does not pick another GPU.
+    """
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.01
+    # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*).
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4))
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.file = None
+        self.nvml = None
+        self.handle = None
+        self.rows: list[dict] = []
+        self.stop = None
+        self.thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _nvml_sample(self) -> None:
+        nv, h = self.nvml, self.handle
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.rows.append({"sm": float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                          "max": float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)),
+                          "power": nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                          "reasons": [name for name, bit in self.REASON_BITS if reasons & bit]})
+
+    def _poll(self) -> None:
+        while not self.stop.wait(self.PERIOD_S):
+            try:
+                self._nvml_sample()
+            except Exception:
+                return
 
     def __enter__(self):
+        try:
+            self.handle = self._nvml_handle()
+            self._nvml_sample()
+            import threading
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.handle = None
+            self.rows = []
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
@@ -128,6 +181,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -135,9 +191,9 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self) -> dict | None:
+    def _smi_rows(self) -> list[dict]:
         if self.proc is None or self.file is None:
-            return None
+            return []
         self.file.flush()
         rows = []
         for line in Path(self.file.name).read_text().splitlines():
@@ -145,22 +201,23 @@ class ClockSampler:
             if len(parts) < 9:
                 continue
             try:
+                flags = dict(zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 parts[5:9]))
                 rows.append({"sm": float(parts[1]), "max": float(parts[2]), "power": float(parts[3]),
-                             "active": parts[4], "hw": parts[5], "hw_thermal": parts[6],
-                             "sw_thermal": parts[7], "sw_power": parts[8]})
+                             "reasons": [k for k, v in flags.items() if v.lower() == "active"]})
             except ValueError:
                 continue
         os.unlink(self.file.name)
+        return rows
+
+    def summary(self) -> dict | None:
+        rows = self.rows if self.handle is not None else self._smi_rows()
         if not rows:
             return None
-        reasons = set()
-        for r in rows:
-            for key, name in (("hw", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
-                              ("sw_thermal", "sw_thermal_slowdown"), ("sw_power", "sw_power_cap")):
-                if r[key].lower() == "active":
-                    reasons.add(name)
+        reasons = sorted({r for row in rows for r in row["reasons"]})
         return {"sm_mhz": statistics.median(r["sm"] for r in rows), "sm_max_mhz": max(r["max"] for r in rows),
-                "power_w_max": max(r["power"] for r in rows), "samples": len(rows), "reasons": sorted(reasons)}
+                "power_w_max": max(r["power"] for r in rows), "samples": len(rows), "reasons": reasons,
+                "source": "nvml" if self.handle is not None else "nvidia-smi"}
 
 
 def host_threads() -> int:
