@@ -545,6 +545,10 @@ int run(const Options& o) {
   CUDA_OK(cudaDriverGetVersion(&drv));
   const size_t ws_bytes = lt ? lt->ws_bytes : partial.bytes;
   const double tflops = 2.0 * static_cast<double>(o.m) * o.n * o.k / (st.p50 * 1e-3) / 1e12;
+  // Algorithmic HBM bytes of one call: A, B and C each moved once.
+  const double bytes = static_cast<double>(sizeof(T)) *
+                       (static_cast<double>(o.m) * o.k + static_cast<double>(o.k) * o.n + static_cast<double>(o.m) * o.n);
+  const double gbs = bytes / (st.p50 * 1e-3) / 1e9;
 
   const char* nl = o.pretty ? "\n" : "";
   const char* i1 = o.pretty ? "  " : "";
@@ -571,7 +575,8 @@ int run(const Options& o) {
     << ",\"sample_inner_repetitions\":" << inner << ",\"measurement_min_seconds\":" << o.measurement_seconds
     << ",\"workspace_bytes\":" << ws_bytes << ",\"split_k\":" << splits << ",\"latency_ms\":{\"p05\":" << st.p05
     << ",\"p50\":" << st.p50 << ",\"p95\":" << st.p95 << ",\"mean\":" << st.mean << ",\"stddev\":" << st.stddev
-    << ",\"mad\":" << st.mad << ",\"cv\":" << st.cv << "},\"tflops_p50\":" << tflops << ",\"raw_ms\":[";
+    << ",\"mad\":" << st.mad << ",\"cv\":" << st.cv << "},\"tflops_p50\":" << tflops
+    << ",\"algorithmic_bytes\":" << bytes << ",\"gbs_p50\":" << gbs << ",\"raw_ms\":[";
   for (size_t i = 0; i < ms.size(); ++i) j << (i ? "," : "") << ms[i];
   j << "]}" << nl << '}' << '\n';
   std::cout << j.str();

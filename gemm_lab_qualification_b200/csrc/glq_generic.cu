@@ -6,7 +6,9 @@
 // pitches that are not a multiple of 16 bytes such as K = 4090).  A 32 x 64
 // output tile per 256-thread CTA; A and B tiles are staged through shared
 // memory in FP32 with the unit-stride dimension mapped to consecutive
-// threads, and every thread accumulates its 2 x 4 outputs in ascending k.
+// threads (each tile's loads issued together into registers, the next tile
+// prefetched during the current one's products), and every thread
+// accumulates its 2 x 4 outputs in ascending k.
 // Reference counterpart: the masked-load tile loop of _matmul_kernel
 // (kernels.py:103-129), which the lab only reaches for contiguous inputs
 // (kernels.py:143-144); strided views fell back to torch there
@@ -56,6 +58,53 @@ struct GenericArgs {
 };
 
 constexpr int kBM = 32, kBN = 64, kBK = 32, kThreads = 256;
+constexpr int kALoads = kBM * kBK / kThreads;  // A elements a thread stages per k tile
+constexpr int kBLoads = kBN * kBK / kThreads;  // B elements a thread stages per k tile
+
+// One k tile of A and B held in registers between its global loads and its
+// shared-memory stores.  All loads of a tile are issued back to back (fully
+// unrolled, no store in between), so a tile costs one memory latency rather
+// than one per element; the next tile's loads are in flight while the
+// current one is multiplied.
+struct TileRegs {
+  float a[kALoads];
+  float b[kBLoads];
+};
+
+template <typename T>
+__device__ __forceinline__ void load_tile(const GenericArgs& g, const T* a, const T* b, long long m0, long long n0,
+                                          long long k0, int tid, TileRegs& r) {
+#pragma unroll
+  for (int j = 0; j < kALoads; ++j) {
+    const int i = tid + j * kThreads;
+    const int row = g.a_k_fast ? i / kBK : i % kBM;
+    const int col = g.a_k_fast ? i % kBK : i / kBM;
+    const long long m = m0 + row, kk = k0 + col;
+    r.a[j] = (m < g.m && kk < g.k) ? Conv<T>::to_f(a[m * g.a_rs + kk * g.a_cs]) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < kBLoads; ++j) {
+    const int i = tid + j * kThreads;
+    const int row = g.b_k_fast ? i / kBK : i % kBN;
+    const int col = g.b_k_fast ? i % kBK : i / kBN;
+    const long long nn = n0 + row, kk = k0 + col;
+    r.b[j] = (nn < g.n && kk < g.k) ? Conv<T>::to_f(b[kk * g.b_ks + nn * g.b_ns]) : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void store_tile(const GenericArgs& g, const TileRegs& r, int tid,
+                                           float (*As)[kBM + 1], float (*Bs)[kBN + 1]) {
+#pragma unroll
+  for (int j = 0; j < kALoads; ++j) {
+    const int i = tid + j * kThreads;
+    As[g.a_k_fast ? i % kBK : i / kBM][g.a_k_fast ? i / kBK : i % kBM] = r.a[j];
+  }
+#pragma unroll
+  for (int j = 0; j < kBLoads; ++j) {
+    const int i = tid + j * kThreads;
+    Bs[g.b_k_fast ? i % kBK : i / kBN][g.b_k_fast ? i / kBK : i % kBN] = r.b[j];
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) generic_kernel(const GenericArgs g) {
@@ -70,32 +119,12 @@ __global__ void __launch_bounds__(kThreads) generic_kernel(const GenericArgs g) 
   const T* b = static_cast<const T*>(g.b);
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 
+  TileRegs regs;
+  load_tile<T>(g, a, b, m0, n0, 0, tid, regs);
   for (long long k0 = 0; k0 < g.k; k0 += kBK) {
-    for (int i = tid; i < kBM * kBK; i += kThreads) {
-      int r, c;
-      if (g.a_k_fast) {
-        r = i / kBK;
-        c = i % kBK;
-      } else {
-        c = i / kBM;
-        r = i % kBM;
-      }
-      const long long m = m0 + r, kk = k0 + c;
-      As[c][r] = (m < g.m && kk < g.k) ? Conv<T>::to_f(a[m * g.a_rs + kk * g.a_cs]) : 0.0f;
-    }
-    for (int i = tid; i < kBN * kBK; i += kThreads) {
-      int r, c;
-      if (g.b_k_fast) {
-        r = i / kBK;
-        c = i % kBK;
-      } else {
-        c = i / kBN;
-        r = i % kBN;
-      }
-      const long long nn = n0 + r, kk = k0 + c;
-      Bs[c][r] = (nn < g.n && kk < g.k) ? Conv<T>::to_f(b[kk * g.b_ks + nn * g.b_ns]) : 0.0f;
-    }
+    store_tile(g, regs, tid, As, Bs);
     __syncthreads();
+    if (k0 + kBK < g.k) load_tile<T>(g, a, b, m0, n0, k0 + kBK, tid, regs);
 #pragma unroll 8
     for (int kk = 0; kk < kBK; ++kk) {
       const float a0 = As[kk][tm * 2], a1 = As[kk][tm * 2 + 1];
