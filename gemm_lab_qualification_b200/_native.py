@@ -19,7 +19,8 @@ LIBRARY_PATH = Path(__file__).resolve().parent / "libglq.so"
 # enum glq_dtype / glq_epilogue / glq_path / glq_status (include/glq.h)
 DTYPE_F16, DTYPE_BF16 = 0, 1
 EPILOGUE_NONE, EPILOGUE_BIAS, EPILOGUE_BIAS_SILU = 0, 1, 2
-PATHS = ("empty", "zero_k", "gemv_m1", "tc_tcgen05", "tc_splitk", "tail", "strided", "unaligned", "tc_kn")
+PATHS = ("empty", "zero_k", "gemv_m1", "tc_tcgen05", "tc_splitk", "tail", "strided", "unaligned", "tc_kn",
+         "repacked")
 STATUS_OK = 0
 STATUS_NAMES = ("ok", "invalid_argument", "shape", "split", "workspace", "output_layout", "cuda",
                 "device", "device_timeout", "scratch")
@@ -50,6 +51,7 @@ SIGNATURES = {
                                         _I64, _I64, _I64, _I64, _I64, _INT, _INT, _INT, ctypes.POINTER(_VP),
                                         _INT, ctypes.c_uint64, _VP, ctypes.c_uint, _PINT, _PINT]),
     "glq_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _INT]),
+    "glq_linear_workspace_bytes": (ctypes.c_size_t, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _I64, _I64, _I64]),
     "glq_plan": (_INT, [_INT, _VP, _I64, _I64, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _INT,
                         _PINT, _PINT]),
     "glq_path_name": (ctypes.c_char_p, [_INT]),
@@ -114,6 +116,14 @@ def dtype_code(dtype: torch.dtype) -> int:
 
 def workspace_bytes(m: int, n: int, k: int, split_k: int = 0) -> int:
     return int(library().glq_workspace_bytes(m, n, k, split_k))
+
+
+def linear_workspace_bytes(dtype: int, a_ptr: int, a_strides: tuple[int, int], b_ptr: int,
+                           b_strides: tuple[int, int], m: int, n: int, k: int) -> int:
+    """Workspace with which glq_linear copies strided or unaligned operands
+    into aligned rows and runs the tcgen05 / GEMV kernel (0: not needed)."""
+    return int(library().glq_linear_workspace_bytes(dtype, a_ptr, a_strides[0], a_strides[1], b_ptr, b_strides[0],
+                                                    b_strides[1], m, n, k))
 
 
 def plan(dtype: int, a_ptr: int, a_strides: tuple[int, int], b_ptr: int, b_strides: tuple[int, int],

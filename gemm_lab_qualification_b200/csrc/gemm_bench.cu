@@ -406,7 +406,8 @@ int run(const Options& o) {
 
   // Implementation set-up (never inside the timed region).
   std::unique_ptr<LtPlan> lt;
-  DeviceMem partial, wnk;
+  DeviceMem partial, wnk, repack;
+  int run_path = -1, run_split = 0;  // what the repacked launches report
   int splits = 1, path = -1, plan_split = 1;
   if (o.impl == "cublaslt") lt = std::make_unique<LtPlan>(Type<T>::kCuda, o.m, o.n, o.k);
   if (o.impl == "glq" || o.impl == "glq_splitk") {
@@ -427,6 +428,18 @@ int run(const Options& o) {
     glq_ok(glq_plan(Type<T>::kGlq, da.p, o.k, 1, wnk.p, 1, o.k, o.n, o.m, o.n, o.k, 0, 0, &path, &plan_split),
            "glq_plan");
   }
+  // Row pitches that are not a multiple of 16 bytes (odd K or N): the
+  // library copies the operands into aligned rows in this workspace and runs
+  // the tensor-core kernels (path "repacked") instead of the generic kernel.
+  if (o.impl == "glq" || o.impl == "glq_wnk") {
+    const bool kn = o.impl == "glq";
+    const size_t need = glq_linear_workspace_bytes(Type<T>::kGlq, da.p, o.k, 1, kn ? db.p : wnk.p, kn ? o.n : 1,
+                                                   kn ? 1 : o.k, o.m, o.n, o.k);
+    if (need) {
+      repack = DeviceMem(need);
+      path = GLQ_PATH_REPACKED;
+    }
+  }
 
   auto launch = [&]() {
     if (o.impl == "cublas") {
@@ -435,7 +448,11 @@ int run(const Options& o) {
       lt->run(da.p, db.p, dc.p, stream);
     } else if constexpr (!std::is_same<T, float>::value) {
       const int g = Type<T>::kGlq;
-      if (o.impl == "glq") {
+      if (o.impl == "glq" && repack.p != nullptr) {
+        glq_ok(glq_linear(g, da.p, o.k, 1, db.p, o.n, 1, nullptr, GLQ_EPILOGUE_NONE, dc.p, o.n, o.m, o.n, o.k, 0,
+                          repack.p, repack.bytes, stream, &run_path, &run_split),
+               "glq_linear");
+      } else if (o.impl == "glq") {
         glq_ok(glq_matmul(g, da.p, db.p, dc.p, static_cast<int>(o.m), static_cast<int>(o.n), static_cast<int>(o.k),
                           stream),
                "glq_matmul");
@@ -445,7 +462,7 @@ int run(const Options& o) {
                "glq_splitk_matmul");
       } else {
         glq_ok(glq_linear(g, da.p, o.k, 1, wnk.p, 1, o.k, nullptr, GLQ_EPILOGUE_NONE, dc.p, o.n, o.m, o.n, o.k, 0,
-                          nullptr, 0, stream, nullptr, nullptr),
+                          repack.p, repack.bytes, stream, &run_path, &run_split),
                "glq_linear");
       }
     }
@@ -455,6 +472,10 @@ int run(const Options& o) {
   // cuBLAS, the vendor references at sampled elements against CPU FP64.
   launch();
   CUDA_OK(cudaStreamSynchronize(stream));
+  if (repack.p != nullptr) {
+    path = run_path;
+    plan_split = run_split;
+  }
   std::vector<T> hc(nc);
   CUDA_OK(cudaMemcpy(hc.data(), dc.p, dc.bytes, cudaMemcpyDeviceToHost));
   Check check;

@@ -131,6 +131,76 @@ int static_gather_scratch(unsigned int** out) {
 
 }  // namespace
 
+OperandLayout classify(const Problem& p) {
+  constexpr int64_t esz = 2;
+  OperandLayout L;
+  // W = B^T is K-contiguous (a linear layer's weight) or N-contiguous (the
+  // lab's B = [K, N] row-major); anything else is strided.
+  L.a_unit = p.a_cs == 1 || p.k == 1;
+  L.w_kmajor = p.b_ks == 1 || p.k == 1;
+  L.w_mnmajor = !L.w_kmajor && (p.b_ns == 1 || p.n == 1);
+  // TMA / 128-bit loads: 16-byte aligned bases and row pitches, rows that do
+  // not overlap.
+  L.a_ok = L.a_unit && aligned16(p.a) &&
+           (p.m == 1 || (p.a_rs > 0 && (p.a_rs * esz) % 16 == 0 && p.a_rs >= p.k));
+  L.w_ok = (L.w_kmajor || L.w_mnmajor) && aligned16(p.b) &&
+           (L.w_kmajor ? (p.n == 1 || (p.b_ns > 0 && (p.b_ns * esz) % 16 == 0 && p.b_ns >= p.k))
+                       : (p.b_ks > 0 && (p.b_ks * esz) % 16 == 0 && p.b_ks >= p.n));
+  return L;
+}
+
+bool repack_plan(const Problem& p, RepackPlan* r) {
+  *r = RepackPlan();
+  // Small problems run the small kernel on the operands as they are.
+  if (p.m <= 0 || p.n <= 0 || p.k <= 0 || small_problem(p.m, p.n, p.k)) return false;
+  const OperandLayout L = classify(p);
+  auto bytes = [](int64_t rows, int64_t cols) {
+    return (static_cast<size_t>(rows) * static_cast<size_t>(repack_pitch(cols)) * 2u + 255u) / 256u * 256u;
+  };
+  r->a = !L.a_ok;
+  r->w = !L.w_ok;
+  r->w_mn = L.w_mnmajor;
+  if (r->a) r->a_bytes = bytes(p.m, p.k);
+  if (r->w) r->w_bytes = r->w_mn ? bytes(p.k, p.n) : bytes(p.n, p.k);
+  return r->a || r->w;
+}
+
+Problem repacked_problem(const Problem& p, const RepackPlan& r, void* workspace) {
+  Problem q = p;
+  unsigned char* base = static_cast<unsigned char*>(workspace);
+  if (r.a) {
+    q.a = base;
+    q.a_rs = repack_pitch(p.k);
+    q.a_cs = 1;
+  }
+  if (r.w) {
+    q.b = base + r.a_bytes;
+    if (r.w_mn) {
+      q.b_ks = repack_pitch(p.n);
+      q.b_ns = 1;
+    } else {
+      q.b_ks = 1;
+      q.b_ns = repack_pitch(p.k);
+    }
+    // The copy is written by the kernel just before: the GEMM must not read
+    // W ahead of its grid-dependency wait.
+    q.flags &= ~static_cast<unsigned int>(GLQ_FLAG_STATIC_WEIGHTS);
+  }
+  return q;
+}
+
+cudaError_t launch_repacks(const Problem& p, const RepackPlan& r, void* workspace, int sm_count, cudaStream_t s) {
+  unsigned char* base = static_cast<unsigned char*>(workspace);
+  cudaError_t e = cudaSuccess;
+  if (r.a) e = launch_repack(p.a, p.m, p.k, p.a_rs, p.a_cs, base, sm_count, s);
+  if (e == cudaSuccess && r.w) {
+    // K-contiguous copy [N, K] unless B is N-contiguous ([K, N] copy).
+    e = r.w_mn ? launch_repack(p.b, p.k, p.n, p.b_ks, p.b_ns, base + r.a_bytes, sm_count, s)
+               : launch_repack(p.b, p.n, p.k, p.b_ns, p.b_ks, base + r.a_bytes, sm_count, s);
+  }
+  return e;
+}
+
 int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->split = 1;
   c->tile_t = 0;
@@ -147,31 +217,19 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
     c->kernel = kKernelFill;
     return GLQ_OK;
   }
-  constexpr int64_t esz = 2;
-  // W = B^T is K-contiguous (a linear layer's weight) or N-contiguous (the
-  // lab's B = [K, N] row-major); anything else goes to the generic kernel.
-  const bool a_unit = p.a_cs == 1 || p.k == 1;
-  const bool w_kmajor = p.b_ks == 1 || p.k == 1;
-  const bool w_mnmajor = !w_kmajor && (p.b_ns == 1 || p.n == 1);
-  if (!a_unit || (!w_kmajor && !w_mnmajor)) {
+  const OperandLayout L = classify(p);
+  if (!L.a_unit || (!L.w_kmajor && !L.w_mnmajor)) {
     c->path = GLQ_PATH_STRIDED;
-    c->kernel = kKernelGeneric;
+    c->kernel = small_problem(p.m, p.n, p.k) ? kKernelSmall : kKernelGeneric;
     return GLQ_OK;
   }
-  // TMA / 128-bit loads: 16-byte aligned bases and row pitches, rows that do
-  // not overlap.
-  const bool w_ok =
-      aligned16(p.b) &&
-      (w_kmajor ? (p.n == 1 || (p.b_ns > 0 && (p.b_ns * esz) % 16 == 0 && p.b_ns >= p.k))
-                : (p.b_ks > 0 && (p.b_ks * esz) % 16 == 0 && p.b_ks >= p.n));
-  const bool a_ok = aligned16(p.a) && (p.m == 1 || (p.a_rs > 0 && (p.a_rs * esz) % 16 == 0 && p.a_rs >= p.k));
-  if (!w_ok || !a_ok) {
+  if (!L.w_ok || !L.a_ok) {
     c->path = GLQ_PATH_UNALIGNED;
-    c->kernel = kKernelGeneric;
+    c->kernel = small_problem(p.m, p.n, p.k) ? kKernelSmall : kKernelGeneric;
     return GLQ_OK;
   }
-  c->w_mn = w_mnmajor ? 1 : 0;
-  if (p.m == 1 && w_kmajor && !p.require_tc) {
+  c->w_mn = L.w_mnmajor ? 1 : 0;
+  if (p.m == 1 && L.w_kmajor && !p.require_tc) {
     const int sms = sm_count > 0 ? sm_count : 148;
     // The ring GEMV holds a whole SM per CTA, so with static weights (where a
     // call's weight stream should start while its predecessor drains) the
@@ -302,12 +360,26 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   if (v != GLQ_OK) return v;
   v = glq::plan_problem(p, split_k, dev->sm_count, &c);
   if (v != GLQ_OK) return v;
-  if (workspace != nullptr && c.split > 1) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Strided or unaligned operands with a workspace that holds their aligned
+  // copies: repack, then plan the copies (tcgen05 / GEMV instead of the
+  // generic kernel).
+  glq::RepackPlan rp;
+  const bool repack = c.kernel == glq::kKernelGeneric && workspace != nullptr && glq::aligned16(workspace) &&
+                      glq::repack_plan(p, &rp) && workspace_bytes >= rp.bytes();
+  if (repack) {
+    if (glq::launch_repacks(p, rp, workspace, dev->sm_count, s) != cudaSuccess) {
+      cudaGetLastError();
+      return GLQ_ERR_CUDA;
+    }
+    p = glq::repacked_problem(p, rp, workspace);
+    v = glq::plan_problem(p, split_k, dev->sm_count, &c);
+    if (v != GLQ_OK) return v;
+  } else if (workspace != nullptr && c.split > 1) {
     const size_t need = static_cast<size_t>(c.split) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
     if (workspace_bytes < need) return GLQ_ERR_WORKSPACE;
     p.partial = static_cast<float*>(workspace);
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
@@ -317,15 +389,35 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
       e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, nullptr, dev->error_word, s);
       break;
     case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
+    case glq::kKernelSmall: e = glq::launch_small(p, s); break;
     default: break;
   }
   if (e != cudaSuccess) {
     cudaGetLastError();
     return GLQ_ERR_CUDA;
   }
-  if (path_out) *path_out = c.path;
-  if (split_out) *split_out = c.kernel == glq::kKernelGeneric ? 1 : c.split;
+  if (path_out) *path_out = repack ? GLQ_PATH_REPACKED : c.path;
+  if (split_out) *split_out = (c.kernel == glq::kKernelGeneric || c.kernel == glq::kKernelSmall) ? 1 : c.split;
   return GLQ_OK;
+}
+
+size_t glq_linear_workspace_bytes(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride,
+                                  const void* B, int64_t b_k_stride, int64_t b_n_stride, int64_t M, int64_t N,
+                                  int64_t K) {
+  if (glq::validate(dtype, GLQ_EPILOGUE_NONE, M, N, K, 0) != GLQ_OK) return 0;
+  Problem p = {};
+  p.dtype = dtype;
+  p.a = A;
+  p.a_rs = a_row_stride;
+  p.a_cs = a_col_stride;
+  p.b = B;
+  p.b_ks = b_k_stride;
+  p.b_ns = b_n_stride;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  glq::RepackPlan rp;
+  return glq::repack_plan(p, &rp) ? rp.bytes() : 0;
 }
 
 int glq_linear_gather(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride, const void* B,
@@ -479,6 +571,7 @@ const char* glq_path_name(int path) {
     case GLQ_PATH_STRIDED: return "strided";
     case GLQ_PATH_UNALIGNED: return "unaligned";
     case GLQ_PATH_TC_KN: return "tc_kn";
+    case GLQ_PATH_REPACKED: return "repacked";
     default: return "unknown";
   }
 }

@@ -15,10 +15,21 @@
 // (qualification.py:58-64).
 //
 // fill_kernel: K = 0 makes every sum empty, so Y = epilogue(0 [+ bias]).
+//
+// repack_rows_kernel / repack_strided_kernel: with a caller workspace, an
+// operand the TMA kernels cannot address (row pitch or base not 16-byte
+// aligned, or no unit-stride dimension) is first copied into a dense buffer
+// whose rows start on 16-byte boundaries; the tcgen05 or GEMV kernel then
+// reads the copy.  The copy is one HBM read of the operand, and its writes
+// mostly stay in L2 for the GEMM that follows.
+#include <algorithm>
+#include <cstdint>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "glq_internal.h"
+#include "glq_ptx.cuh"
 
 namespace glq {
 namespace {
@@ -35,6 +46,8 @@ struct Conv<__nv_bfloat16> {
   __device__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   __device__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
 };
+
+__device__ __forceinline__ long long abs_ll_dev(long long v) { return v < 0 ? -v : v; }
 
 __device__ __forceinline__ float apply_epilogue(float acc, float bias, int epilogue) {
   if (epilogue == GLQ_EPILOGUE_NONE) return acc;
@@ -165,6 +178,156 @@ __global__ void fill_kernel(T* y, long long ldy, long long m, long long n, const
   }
 }
 
+// small_kernel: problems of at most kSmallMacs multiply-adds in any layout.
+// Latency, not bandwidth, bounds them, so K is spread over many threads and
+// every thread's loads are independent (one or two memory round trips):
+//  LANES_N: B has the smaller stride along n (e.g. the lab's B = [K, N]): a
+//    CTA owns 32 consecutive outputs of one row, lane = output, and its 8
+//    warps take interleaved eighths of K; the 8 partial sums are added in
+//    warp order through shared memory.
+//  !LANES_N: one warp per output, lane j takes k = j, j + 32, ...; the lane
+//    sums are combined by a fixed xor-butterfly.
+// Both orders are fixed, so repeated calls give identical bits.
+template <typename T, bool LANES_N>
+__global__ void __launch_bounds__(256) small_kernel(const GenericArgs g) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* a = static_cast<const T*>(g.a);
+  const T* b = static_cast<const T*>(g.b);
+  const long long m = blockIdx.y;
+  long long n;
+  float acc = 0.0f;
+  if constexpr (LANES_N) {
+    __shared__ float part[8][32];
+    n = static_cast<long long>(blockIdx.x) * 32 + lane;
+    if (n < g.n) {
+      const T* arow = a + m * g.a_rs;
+      const T* bcol = b + n * g.b_ns;
+#pragma unroll 4
+      for (long long kk = warp; kk < g.k; kk += 8) {
+        acc = fmaf(Conv<T>::to_f(arow[kk * g.a_cs]), Conv<T>::to_f(bcol[kk * g.b_ks]), acc);
+      }
+    }
+    part[warp][lane] = acc;
+    __syncthreads();
+    if (warp != 0 || n >= g.n) return;
+    acc = part[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) acc += part[w][lane];
+  } else {
+    n = static_cast<long long>(blockIdx.x) * 8 + warp;
+    if (n >= g.n) return;
+    const T* arow = a + m * g.a_rs;
+    const T* bcol = b + n * g.b_ns;
+#pragma unroll 4
+    for (long long kk = lane; kk < g.k; kk += 32) {
+      acc = fmaf(Conv<T>::to_f(arow[kk * g.a_cs]), Conv<T>::to_f(bcol[kk * g.b_ks]), acc);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane != 0) return;
+  }
+  float bias_v = 0.0f;
+  if (g.epilogue != GLQ_EPILOGUE_NONE) bias_v = Conv<T>::to_f(static_cast<const T*>(g.bias)[n]);
+  static_cast<T*>(g.y)[m * g.ldy + n] = Conv<T>::from_f(apply_epilogue(acc, bias_v, g.epilogue));
+}
+
+// One thread per 16-byte output chunk (8 elements) of a row whose elements
+// are contiguous.  The chunk's source bytes lie in the aligned granule that
+// holds its first element and, unless that element starts the granule, the
+// next granule; the 32-byte window is shifted right by the byte offset.  A
+// granule is read only if it holds at least one byte of this row (the first
+// always does; the second is skipped past the row's end), and an aligned
+// 16-byte granule never crosses a page, so no read leaves the operand's
+// pages.  Columns >= cols are written as zero.
+__global__ void __launch_bounds__(256) repack_rows_kernel(const unsigned char* src, long long rows, long long cols,
+                                                          long long stride_bytes, uint4* dst,
+                                                          long long pitch_chunks) {
+  ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
+  const long long total = rows * pitch_chunks;
+  for (long long idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += static_cast<long long>(gridDim.x) * 256) {
+    const long long r = idx / pitch_chunks;
+    const long long c = idx - r * pitch_chunks;
+    const long long col0 = c * 8;
+    uint32_t out[4] = {0u, 0u, 0u, 0u};
+    if (col0 < cols) {
+      const uintptr_t row_begin = reinterpret_cast<uintptr_t>(src) + static_cast<uintptr_t>(r * stride_bytes);
+      const uintptr_t row_end = row_begin + static_cast<uintptr_t>(cols) * 2u;
+      const uintptr_t first = row_begin + static_cast<uintptr_t>(col0) * 2u;
+      const uintptr_t g0 = first & ~static_cast<uintptr_t>(15);
+      const unsigned shift = static_cast<unsigned>(first - g0);
+      const uint4 lo = __ldg(reinterpret_cast<const uint4*>(g0));
+      uint4 hi = make_uint4(0u, 0u, 0u, 0u);
+      if (shift != 0 && g0 + 16 < row_end) hi = __ldg(reinterpret_cast<const uint4*>(g0 + 16));
+      const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      const unsigned q = shift >> 2;
+      const unsigned bits = (shift & 3u) * 8u;
+      uint32_t pick[5];
+#pragma unroll
+      for (int j = 0; j < 5; ++j) {
+        // w[j + q] with q in 0..3, j + q <= 7: selects on compile-time indices.
+        const uint32_t x0 = w[j], x1 = w[j + 1 < 8 ? j + 1 : 7], x2 = w[j + 2 < 8 ? j + 2 : 7],
+                       x3 = w[j + 3 < 8 ? j + 3 : 7];
+        pick[j] = q == 0 ? x0 : q == 1 ? x1 : q == 2 ? x2 : x3;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) out[j] = __funnelshift_r(pick[j], pick[j + 1], bits);
+      const long long valid = cols - col0;
+      if (valid < 8) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (2 * j >= valid) {
+            out[j] = 0u;
+          } else if (2 * j + 1 >= valid) {
+            out[j] &= 0xFFFFu;
+          }
+        }
+      }
+    }
+    dst[idx] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+// Any element strides: 32 x 64 tiles through shared memory, read with
+// consecutive threads along the smaller source stride, written as 16-byte
+// chunks along the output row.  Columns >= cols are written as zero.
+constexpr int kRpRows = 32, kRpCols = 64;
+
+__global__ void __launch_bounds__(256) repack_strided_kernel(const uint16_t* src, long long rows, long long cols,
+                                                             long long rs, long long cs, uint4* dst,
+                                                             long long pitch_chunks) {
+  __shared__ uint32_t tile32[kRpRows * (kRpCols / 2 + 1)];
+  uint16_t* const tile = reinterpret_cast<uint16_t*>(tile32);
+  constexpr int kPitch = kRpCols + 2;  // elements per shared row
+  ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
+  const bool cols_fast = abs_ll_dev(cs) <= abs_ll_dev(rs);
+  const long long tiles_c = (pitch_chunks * 8 + kRpCols - 1) / kRpCols;
+  const long long tiles = ((rows + kRpRows - 1) / kRpRows) * tiles_c;
+  for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const long long r0 = (t / tiles_c) * kRpRows;
+    const long long c0 = (t % tiles_c) * kRpCols;
+#pragma unroll
+    for (int j = 0; j < kRpRows * kRpCols / 256; ++j) {
+      const int i = threadIdx.x + j * 256;
+      const int rr = cols_fast ? i / kRpCols : i % kRpRows;
+      const int cc = cols_fast ? i % kRpCols : i / kRpRows;
+      const long long r = r0 + rr, c = c0 + cc;
+      tile[rr * kPitch + cc] = (r < rows && c < cols) ? src[r * rs + c * cs] : static_cast<uint16_t>(0);
+    }
+    __syncthreads();
+    const int rr = threadIdx.x / (kRpCols / 8);
+    const int ch = threadIdx.x % (kRpCols / 8);
+    const long long r = r0 + rr;
+    const long long chunk = c0 / 8 + ch;
+    if (r < rows && chunk < pitch_chunks) {
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(tile + rr * kPitch + ch * 8);
+      dst[r * pitch_chunks + chunk] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __syncthreads();
+  }
+}
+
 long long abs_ll(long long v) { return v < 0 ? -v : v; }
 
 }  // namespace
@@ -191,6 +354,53 @@ cudaError_t launch_generic(const Problem& p, cudaStream_t s) {
     generic_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(g);
   } else {
     generic_kernel<__half><<<grid, kThreads, 0, s>>>(g);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_small(const Problem& p, cudaStream_t s) {
+  GenericArgs g = {};
+  g.a = p.a;
+  g.a_rs = p.a_rs;
+  g.a_cs = p.a_cs;
+  g.b = p.b;
+  g.b_ks = p.b_ks;
+  g.b_ns = p.b_ns;
+  g.bias = p.bias;
+  g.epilogue = p.epilogue;
+  g.y = p.y;
+  g.ldy = p.ldy;
+  g.m = p.m;
+  g.n = p.n;
+  g.k = p.k;
+  const bool lanes_n = abs_ll(p.b_ns) < abs_ll(p.b_ks) && p.n > 1;
+  const dim3 grid(static_cast<unsigned>(lanes_n ? (p.n + 31) / 32 : (p.n + 7) / 8), static_cast<unsigned>(p.m));
+  const bool bf16 = p.dtype == GLQ_DTYPE_BF16;
+  if (lanes_n) {
+    if (bf16) small_kernel<__nv_bfloat16, true><<<grid, 256, 0, s>>>(g);
+    else small_kernel<__half, true><<<grid, 256, 0, s>>>(g);
+  } else {
+    if (bf16) small_kernel<__nv_bfloat16, false><<<grid, 256, 0, s>>>(g);
+    else small_kernel<__half, false><<<grid, 256, 0, s>>>(g);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack(const void* src, int64_t rows, int64_t cols, int64_t rs, int64_t cs, void* dst,
+                          int sm_count, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  const long long pitch_chunks = repack_pitch(cols) / 8;
+  const long long sms = sm_count > 0 ? sm_count : 148;
+  if (cs == 1 || cols == 1) {
+    const long long chunks = rows * pitch_chunks;
+    const long long blocks = std::min<long long>((chunks + 255) / 256, sms * 8);
+    repack_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const unsigned char*>(src), rows, cols, rs * 2, static_cast<uint4*>(dst), pitch_chunks);
+  } else {
+    const long long tiles = ((rows + kRpRows - 1) / kRpRows) * ((pitch_chunks * 8 + kRpCols - 1) / kRpCols);
+    const long long blocks = std::min<long long>(tiles, sms * 8);
+    repack_strided_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const uint16_t*>(src), rows, cols, rs, cs, static_cast<uint4*>(dst), pitch_chunks);
   }
   return cudaGetLastError();
 }

@@ -54,6 +54,29 @@ struct Gather {
   unsigned long long epoch;
 };
 
+// How the operands sit in memory: unit-stride dimensions and whether the
+// TMA kernels can address them (16-byte aligned bases and row pitches, rows
+// that do not overlap).
+struct OperandLayout {
+  bool a_unit = false, a_ok = false;
+  bool w_kmajor = false, w_mnmajor = false, w_ok = false;
+};
+OperandLayout classify(const Problem& p);
+
+// Copies of the operands the TMA kernels cannot address, in a caller
+// workspace: A first ([M, K], K-contiguous), then W (K-contiguous [N, K],
+// or [K, N] when B is N-contiguous), each 256-byte aligned.
+struct RepackPlan {
+  bool a = false, w = false, w_mn = false;
+  size_t a_bytes = 0, w_bytes = 0;
+  size_t bytes() const { return a_bytes + w_bytes; }
+};
+// False when every operand is already TMA-addressable (or nothing to do).
+bool repack_plan(const Problem& p, RepackPlan* r);
+// The same problem reading the copies in `workspace`.
+Problem repacked_problem(const Problem& p, const RepackPlan& r, void* workspace);
+cudaError_t launch_repacks(const Problem& p, const RepackPlan& r, void* workspace, int sm_count, cudaStream_t s);
+
 // Path selection result.
 struct Choice {
   int path;     // glq_path
@@ -72,6 +95,7 @@ enum Kernel : int {
   kKernelTc = 3,
   kKernelGeneric = 4,
   kKernelGemvRing = 5,  // M = 1 GEMV fed by the TMA engine (path gemv_m1)
+  kKernelSmall = 6,     // few multiply-adds, any layout: K spread over warps
 };
 
 // Pure host planning (glq_plan and glq_linear share it).
@@ -126,6 +150,23 @@ inline bool gemv_ring_fits(int64_t n, int64_t k, int sm_count) {
   return fixed + 2 * k * 2 <= 232448;
 }
 cudaError_t launch_generic(const Problem& p, cudaStream_t s);
+// Strided or unaligned problems of at most this many multiply-adds run the
+// small kernel: its latency is a few memory round trips, where the tiled
+// generic kernel walks K in sequence and a repack costs extra launches.
+constexpr int64_t kSmallMacs = int64_t(1) << 22;
+inline bool small_problem(int64_t m, int64_t n, int64_t k) {
+  return m > 0 && n > 0 && k > 0 && m <= 65535 && m * n <= kSmallMacs && m * n * k <= kSmallMacs;
+}
+cudaError_t launch_small(const Problem& p, cudaStream_t s);
+
+// Row pitch (elements) of a repacked operand: rows start on 16-byte
+// boundaries.
+inline int64_t repack_pitch(int64_t cols) { return (cols + 7) / 8 * 8; }
+// Copies rows x cols 2-byte elements, element (r, c) at src + r*rs + c*cs
+// (any alignment), into dst (16-byte aligned) with row pitch
+// repack_pitch(cols); the pad columns are written as zero.
+cudaError_t launch_repack(const void* src, int64_t rows, int64_t cols, int64_t rs, int64_t cs, void* dst,
+                          int sm_count, cudaStream_t s);
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
 // gather: null for a plain call (the output is p.y only).

@@ -70,15 +70,28 @@ std::tuple<int, int, int> linear(const std::string& op, const at::Tensor& a, con
   const int64_t m = a.size(0), k = a.size(1), n = b.size(1);
   if (bias.has_value()) check_bias(*bias, a, n);
   check_output(out, a, m, n);
+  const int dtype = a.scalar_type() == at::kHalf ? GLQ_DTYPE_F16 : GLQ_DTYPE_BF16;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  at::Tensor repack_ws;
   if (partial.has_value()) {
     ws = partial->data_ptr();
     ws_bytes = static_cast<size_t>(partial->numel()) * partial->element_size();
+  } else if (m && n && k) {
+    // Strided or unaligned operands: aligned copies in a workspace from
+    // torch's caching allocator (stream-ordered, so it may be released as
+    // soon as the launches are queued), then the tcgen05 / GEMV kernel.
+    const size_t need = glq_linear_workspace_bytes(dtype, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(),
+                                                   b.stride(0), b.stride(1), m, n, k);
+    if (need) {
+      repack_ws = at::empty({static_cast<int64_t>(need)}, a.options().dtype(at::kByte));
+      ws = repack_ws.data_ptr();
+      ws_bytes = need;
+    }
   }
   const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(a.device().index()).stream();
   int path = -1, split = 0;
-  const int status = glq_linear_ex(a.scalar_type() == at::kHalf ? GLQ_DTYPE_F16 : GLQ_DTYPE_BF16, a.data_ptr(),
+  const int status = glq_linear_ex(dtype, a.data_ptr(),
                                    a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
                                    bias.has_value() ? bias->data_ptr() : nullptr, epilogue, out.data_ptr(),
                                    out.stride(0), m, n, k, split_k, ws, ws_bytes, stream,

@@ -69,11 +69,14 @@ enum glq_path {
   GLQ_PATH_TC = 3,        /* tcgen05 + TMA + TMEM GEMM, no K split */
   GLQ_PATH_TC_SPLITK = 4, /* same, K split across a cluster, DSMEM merge */
   GLQ_PATH_TAIL = 5,      /* tcgen05 or GEMV kernel on a ragged N/K edge */
-  GLQ_PATH_STRIDED = 6,   /* generic kernel: non-unit inner stride */
-  GLQ_PATH_UNALIGNED = 7, /* generic kernel: rows or base not 16-B aligned */
+  GLQ_PATH_STRIDED = 6,   /* generic kernel: non-unit inner stride (no workspace) */
+  GLQ_PATH_UNALIGNED = 7, /* generic kernel: rows or base not 16-B aligned (no workspace) */
   GLQ_PATH_TC_KN = 8,     /* tcgen05 GEMM with an N-contiguous B = [K, N]
                              (the lab's own layout): MN-major W tiles */
-  GLQ_PATH_COUNT = 9
+  GLQ_PATH_REPACKED = 9,  /* strided or unaligned operands copied into the
+                             caller's workspace with 16-B aligned rows, then
+                             the tcgen05 or GEMV kernel on the copies */
+  GLQ_PATH_COUNT = 10
 };
 
 enum glq_status {
@@ -122,7 +125,9 @@ enum glq_flags {
  * workspace: optional (may be NULL).  When non-NULL it receives the FP32
  *   per-split partial sums in the lab's [split, M, N] layout
  *   (kernels.py:431-439), and must hold glq_workspace_bytes() bytes.  The
- *   merge itself never needs it.
+ *   merge itself never needs it.  For operands the TMA kernels cannot
+ *   address, a workspace of glq_linear_workspace_bytes() bytes instead
+ *   holds their aligned copies (GLQ_PATH_REPACKED).
  * path_out, split_out: optional host pointers receiving the path taken and
  *   the split count used.
  *
@@ -193,6 +198,25 @@ int glq_splitk_matmul(int dtype, const void* a, const void* b, void* c,
  * (kernels.py:461-464).  Pure host function.
  */
 size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k);
+
+/*
+ * glq_linear_workspace_bytes -- bytes of workspace with which a glq_linear
+ * call on exactly these operands (pointers and strides) takes the repacked
+ * path: every operand the TMA kernels cannot address (base or row pitch not
+ * 16-byte aligned, overlapping rows, or no unit stride) is first copied into
+ * the workspace with 16-byte aligned rows, and the call then runs the
+ * tcgen05 or GEMV kernel on the copies (path GLQ_PATH_REPACKED).  0 when
+ * the operands are addressable as they are.  Given less, such a call runs
+ * the generic kernel (GLQ_PATH_STRIDED / GLQ_PATH_UNALIGNED), as it does
+ * when the workspace is not 16-byte aligned.  When the
+ * workspace serves a repack it holds no split partials.  Pure host function.
+ * No counterpart in the reference: the lab's Triton kernel reads any
+ * contiguous layout through masked loads (kernels.py:103-129) and sends
+ * strided views to torch (qualification.py:58-64).
+ */
+size_t glq_linear_workspace_bytes(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride,
+                                  const void* B, int64_t b_k_stride, int64_t b_n_stride, int64_t M,
+                                  int64_t N, int64_t K);
 
 /*
  * glq_plan -- the path and split a glq_linear call with these arguments

@@ -12,6 +12,7 @@ import re
 import subprocess
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -153,6 +154,87 @@ def test_workspace_bytes():
     assert native.workspace_bytes(32, 4096, 4096, 1) == 0
     assert native.workspace_bytes(0, 4096, 4096, 4) == 0
     assert native.workspace_bytes(32, 4096, 4096, 9) == 0
+
+
+def repack_bytes(m, n, k, a_strides=None, b_strides=None, a_ptr=0, b_ptr=0):
+    a_strides = a_strides or (k, 1)
+    b_strides = b_strides or (1, k)
+    return native.linear_workspace_bytes(native.DTYPE_F16, a_ptr, a_strides, b_ptr, b_strides, m, n, k)
+
+
+def padded(rows, cols):
+    """Bytes of one aligned copy: rows of ceil(cols / 8) * 8 FP16, 256-B rounded."""
+    return -(-rows * (-(-cols // 8) * 8) * 2 // 256) * 256
+
+
+def test_linear_workspace_bytes():
+    # TMA-addressable operands need no copy.
+    assert repack_bytes(32, 4096, 4096) == 0
+    assert repack_bytes(32, 4096, 4096, b_strides=(4096, 1)) == 0
+    assert repack_bytes(32, 4096, 4090, a_strides=(4096, 1), b_strides=(1, 4096)) == 0
+    # K = 4090 contiguous: both row pitches (8180 B) are unaligned.
+    assert repack_bytes(32, 4096, 4090) == padded(32, 4090) + padded(4096, 4090)
+    # only the operand that is off: a base two bytes off, a transposed A.
+    assert repack_bytes(32, 4096, 4096, a_ptr=2) == padded(32, 4096)
+    assert repack_bytes(1, 4096, 4096, b_ptr=2) == padded(4096, 4096)
+    assert repack_bytes(32, 4096, 4096, a_strides=(1, 32)) == padded(32, 4096)
+    # B = [K, N] with N = 4093: the copy keeps B N-contiguous ([K, N] rows).
+    assert repack_bytes(32, 4093, 4096, b_strides=(4093, 1)) == padded(4096, 4093)
+    # no unit stride in B: copied K-contiguous.
+    assert repack_bytes(32, 4096, 4096, b_strides=(2, 8192)) == padded(4096, 4096)
+    # a wider tail shape, both operands row-major with odd pitches.
+    assert repack_bytes(64, 2055, 131, b_strides=(2055, 1)) == padded(64, 131) + padded(131, 2055)
+    # small problems (<= 2^22 multiply-adds, e.g. the lab's 17 x 257 x 131
+    # tail) run the small kernel on the operands as they are: no copy.
+    assert repack_bytes(17, 257, 131, b_strides=(257, 1)) == 0
+    assert repack_bytes(1, 4096, 1023) == 0
+    assert repack_bytes(1, 4096, 1025) > 0
+    # nothing to compute, or invalid arguments.
+    assert repack_bytes(0, 4096, 4090) == 0
+    assert repack_bytes(32, 4096, 0) == 0
+    assert native.linear_workspace_bytes(7, 0, (4090, 1), 0, (1, 4090), 32, 4096, 4090) == 0
+
+
+def repack_chunk(row: bytes, col0: int, cols: int, base: int) -> bytes:
+    """Host restatement of one 16-byte output chunk of repack_rows_kernel.
+
+    `row` holds the bytes of the aligned granules around a row that starts at
+    address `base` (the row's first byte is row[base % 16]); the chunk of
+    columns col0 .. col0 + 7 comes from the granule holding its first byte
+    and the next one, shifted by the byte offset, columns >= cols zeroed.
+    """
+    first = base + 2 * col0
+    g0 = first - first % 16
+    shift = first - g0
+    end = base + 2 * cols
+    origin = base - base % 16  # address of row[0]
+    lo = row[g0 - origin:g0 - origin + 16]
+    hi = row[g0 + 16 - origin:g0 + 32 - origin] if shift and g0 + 16 < end else bytes(16)
+    words = [int.from_bytes((lo + hi)[4 * i:4 * i + 4], "little") for i in range(8)]
+    q, bits = shift >> 2, (shift & 3) * 8
+    pick = [words[j + q] for j in range(5)]
+    out = [((pick[j + 1] << 32 | pick[j]) >> bits) & 0xFFFFFFFF for j in range(4)]
+    valid = cols - col0
+    for j in range(4):
+        if 2 * j >= valid:
+            out[j] = 0
+        elif 2 * j + 1 >= valid:
+            out[j] &= 0xFFFF
+    return b"".join(w.to_bytes(4, "little") for w in out)
+
+
+@pytest.mark.parametrize("cols", [1, 7, 8, 9, 131, 4090])
+def test_repack_window_restatement(cols):
+    """Every byte offset of a row start (even offsets for 2-byte elements and
+    odd ones too) gives the row's elements, zero-padded to a multiple of 8."""
+    rng = np.random.default_rng(cols)
+    for base in range(1024, 1040):
+        start = base % 16
+        span = -(-(start + 2 * cols) // 16) * 16 + 16
+        row = rng.integers(0, 256, size=span, dtype=np.uint8).tobytes()
+        expected = row[start:start + 2 * cols] + bytes(2 * (-(-cols // 8) * 8 - cols))
+        got = b"".join(repack_chunk(row, c, cols, base) for c in range(0, cols, 8))
+        assert got == expected
 
 
 def test_linear_validation_precedes_device_use():
