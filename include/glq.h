@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define GLQ_ABI_VERSION 2
+#define GLQ_ABI_VERSION 3
 
 /* Element types (inputs, bias and output share one type). */
 enum glq_dtype {

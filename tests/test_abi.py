@@ -43,7 +43,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_abi_version_and_target():
     lib = native.library()
-    assert lib.glq_abi_version() == 2
+    assert lib.glq_abi_version() == 3
     assert lib.glq_build_target() == b"sm_100a"
 
 
