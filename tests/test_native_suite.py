@@ -151,3 +151,20 @@ def test_suite_on_the_device(cuda_device, tmp_path):
     native_suite.save(target, doc)
     text = summarize.render(json.loads(target.read_text()))
     assert "| decode-m32 |" in text and "| tail |" in text
+
+
+def test_command_lines(tmp_path, capsys):
+    cli, _ = fake_cli(tmp_path)
+    suite = tmp_path / "suite.json"
+    assert native_suite.main(["--output", str(suite), "--binary", str(cli), "--rounds", "1", "--impls",
+                              "cublaslt,glq", "--cache", "steady"]) == 0
+    doc = json.loads(suite.read_text())
+    assert {r["record"]["implementation"]["name"] for r in doc["results"]} == {"cublaslt", "glq"}
+    assert len(doc["results"]) == 2 * len(native_suite.MANIFEST["benchmark"])
+    report = tmp_path / "report.md"
+    assert summarize.main([str(suite), "--output", str(report)]) == 0
+    assert "| decode-m32 |" in report.read_text() and "Cache mode: cold" not in report.read_text()
+    assert summarize.main([str(suite)]) == 0
+    assert "# B200 measurements" in capsys.readouterr().out
+    with pytest.raises(SystemExit):
+        summarize.main([])
