@@ -70,6 +70,10 @@ class ColumnParallelLinear:
             raise ValueError("the fused SiLU epilogue takes a bias")
         self.activation = activation
         self.n, self.k = weight.shape
+        if fused_gather and self.k % 8 != 0:
+            # The gather is fused into the tcgen05 kernel, which reads A and W
+            # through TMA: rows must be 16-byte pitched.
+            raise ValueError("the fused gather needs K to be a multiple of 8 (16-byte rows of A and W)")
         device = device if device is not None else weight.device
         self.weight = shard_rows(weight, self.rank, self.world).to(device).contiguous()
         self.bias = shard_rows(bias, self.rank, self.world).to(device).contiguous() if bias is not None else None

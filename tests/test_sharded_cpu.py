@@ -46,6 +46,10 @@ def worker(rank: int, world: int, port: int, m: int, n: int, k: int, errors) -> 
         assert np.array_equal(out.numpy(), full), "gathered layout differs from the unsharded result"
         with pytest.raises(ValueError):
             sharded.shard_rows(torch.zeros(n + 1, 2), rank, world)
+        # the fused gather needs 16-byte rows: refused before any device work
+        with pytest.raises(ValueError, match="multiple of 8"):
+            sharded.ColumnParallelLinear(torch.zeros(n, 13, dtype=torch.float16), torch.zeros(n, dtype=torch.float16),
+                                         device=torch.device("cpu"), fused_gather=True)
         dist.barrier()
     except BaseException as exc:  # report to the parent, never hang it
         errors.put(f"rank {rank}: {exc!r}")
