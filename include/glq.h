@@ -224,6 +224,9 @@ size_t glq_linear_workspace_bytes(int dtype, const void* A, int64_t a_row_stride
  * arguments are only inspected for alignment).  Replaces the per-call path
  * selection of qualification.path (qualification.py:58-59) and
  * ptx_mma_split_count (csrc/ptx_mma.cuh:889-924).  sm_count 0 = 148.
+ * It plans a call without workspace: for operands that a workspace of
+ * glq_linear_workspace_bytes() bytes would repack, it reports
+ * GLQ_PATH_STRIDED / GLQ_PATH_UNALIGNED.
  */
 int glq_plan(int dtype,
              const void* A, int64_t a_row_stride, int64_t a_col_stride,
