@@ -70,6 +70,7 @@ def parse_args(argv=None):
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-probes", action="store_true", help="skip the boundary and split-K probe timings")
     p.add_argument("--inner", type=int, default=10, help="back-to-back calls per timed sample")
     p.add_argument("--sweep", type=str, default=",".join(map(str, SWEEP_M)),
                    help="comma-separated M values of the step (default 1,8,32,128)")
@@ -499,6 +500,80 @@ def single_gpu(args, torch, dev) -> dict:
             "gpu_launches": args.steps * len(fns) * args.inner, "state": state}
 
 
+PROBE_A_VIEWS = {"a_padded": "padded", "a_transposed": "transposed", "a_offset": "offset"}
+
+
+def probe_timings(args, torch, dev) -> dict:
+    """The manifest's boundary probes and the forced split-K probes, timed.
+
+    Each probe runs through the operator API (triton_bias_silu_into, or
+    triton_splitk_matmul_into with a caller FP32 [S, M, N] partial buffer) and
+    is timed like the sweep: p50 of `inner` back-to-back calls behind a GPU
+    hold, the weight rotating over copies larger than L2.  GB/s counts the
+    algorithmic bytes; the split partials' write-back is inside the timed
+    region but not counted.
+    """
+    from gemm_lab_qualification_b200 import kernels, workloads
+    from gemm_lab_qualification_b200.evidence import device_measure
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    peak, _ = measured_hbm_peak()
+    rounds = max(10, args.steps // 10)
+
+    def copies_for(nbytes: int) -> int:
+        return max(2, -(-2 * l2 // nbytes) + 1) if nbytes else 1
+
+    def measure(fn) -> float:
+        fn()
+        device_measure({"p": fn}, rounds=2, inner=args.inner)
+        return statistics.median(device_measure({"p": fn}, rounds=rounds, inner=args.inner)["p"]) * 1e3
+
+    boundary = []
+    for probe in workloads.MANIFEST["probes"]:
+        m, n, k, layout = probe["m"], probe["n"], probe["k"], probe["layout"]
+        a, w, bias = workloads.uniform_inputs(m, n, k)
+        da = workloads.poisoned_view(a, PROBE_A_VIEWS[layout], dev) if layout in PROBE_A_VIEWS else a.to(dev)
+        copies = copies_for(w.numel() * 2)
+        wts = [workloads.poisoned_view(w, "padded", dev) if layout == "w_padded" else w.to(dev)
+               for _ in range(copies)]
+        db = bias.to(dev)
+        y = torch.empty((m, n), dtype=torch.float16, device=dev)
+        cnt = {"i": 0}
+
+        def call(da=da, wts=wts, db=db, y=y, cnt=cnt):
+            cnt["i"] += 1
+            kernels.triton_bias_silu_into(da, wts[cnt["i"] % len(wts)].t(), db, y)
+        us = measure(call)
+        path = kernels.last_path()
+        nbytes = algorithmic_bytes(m, n, k) if m and n else 0
+        gbs = nbytes / (us * 1e-6) / 1e9 if nbytes and us > 0 else None
+        boundary.append({"id": probe["id"], "m": m, "n": n, "k": k, "layout": layout, "path": path[0],
+                         "split": path[1], "p50_us": us, "gbs": gbs, "frac": gbs / peak if gbs else None})
+        del wts
+    split = []
+    sp = workloads.MANIFEST["split_probes"]
+    _, w, _ = workloads.uniform_inputs(1, sp["n"], sp["k"])
+    wts = [w.to(dev) for _ in range(copies_for(w.numel() * 2))]
+    for m in sp["m"]:
+        a, _, _ = workloads.uniform_inputs(m, sp["n"], sp["k"])
+        da = a.to(dev)
+        y = torch.empty((m, sp["n"]), dtype=torch.float16, device=dev)
+        for s in sp["splits"]:
+            partial = torch.empty((s, m, sp["n"]), dtype=torch.float32, device=dev)
+            cnt = {"i": 0}
+
+            def call(da=da, partial=partial, y=y, s=s, cnt=cnt):
+                cnt["i"] += 1
+                kernels.triton_splitk_matmul_into(da, wts[cnt["i"] % len(wts)].t(), partial, y, s)
+            us = measure(call)
+            path = kernels.last_path()
+            gbs = algorithmic_bytes(m, sp["n"], sp["k"], bias=False) / (us * 1e-6) / 1e9
+            split.append({"m": m, "split": s, "path": path[0], "reported_split": path[1], "p50_us": us,
+                          "gbs": gbs, "frac": gbs / peak, "partial_bytes": s * m * sp["n"] * 4})
+    del wts
+    return {"protocol": f"operator API, p50 of {args.inner} back-to-back calls behind a GPU hold, {rounds} "
+                        "samples, weight rotating over copies > L2", "boundary": boundary, "split": split}
+
+
 def e2e_public_api(args, torch, dev, rounds: int) -> dict:
     """Host buffers in, host result out, through kernels.triton_bias_silu_into."""
     from gemm_lab_qualification_b200 import kernels, workloads
@@ -816,6 +891,8 @@ def run_native(args) -> int:
                              f"({res['copies'] * 32} MiB) > L2 {res['l2_bytes'] / 2**20:.0f} MiB"},
             "impl": "native", "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
             "clocks": res["clocks"], "sweep": res["sweep"], "mlp_shapes": res["mlp_shapes"]}
+    if not args.no_probes:
+        line["probes"] = probe_timings(args, torch, dev)
     if not args.no_e2e:
         e2e = e2e_public_api(args, torch, dev, rounds=max(10, min(args.steps, 50)))
         line["e2e"] = e2e["all_inputs"]

@@ -229,7 +229,11 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
     return GLQ_OK;
   }
   c->w_mn = L.w_mnmajor ? 1 : 0;
-  if (p.m == 1 && L.w_kmajor && !p.require_tc) {
+  // M = 1 runs a GEMV, except for a forced split of 4 or more: the register
+  // GEMV then holds one or two rows per block and every block re-stages all
+  // of A (19 us at S = 8 vs 9.9 us for the tcgen05 split, which writes the
+  // same [S, 1, N] FP32 partials).
+  if (p.m == 1 && L.w_kmajor && !p.require_tc && split_k < 4) {
     const int sms = sm_count > 0 ? sm_count : 148;
     // The ring GEMV holds a whole SM per CTA, so with static weights (where a
     // call's weight stream should start while its predecessor drains) the

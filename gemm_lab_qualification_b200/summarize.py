@@ -9,7 +9,8 @@ memory-bound B200 row needs: the path the library chose, GB/s of the
 algorithmic bytes, and the fraction of the measured HBM copy bandwidth, for
 the steady (warm-L2) and cold cache modes separately.  With a bench.py JSON
 line it also renders the per-M sweep (device-resident, rotating weights),
-the MLP shapes and the end-to-end (host buffers) number.
+the MLP shapes, the timed boundary and split-K probes and the end-to-end
+(host buffers) number.
 
 ``python -m gemm_lab_qualification_b200.summarize suite.json [--bench
 bench.json] [--peaks MEASURED_PEAKS.json] --output report.md``
@@ -125,6 +126,19 @@ def render_bench(bench: dict) -> list[str]:
             path = r["path"] if isinstance(r["path"], str) else f"{r['path'][0]}/{r['path'][1]}"
             lines.append(f"| {r['m']}×{r['n']}×{r['k']} | {path} | {r['fused_p50_us']:.2f} | {r['gbs']:.0f} | "
                          f"{_fmt(r.get('cublas_fused_p50_us'))} |")
+        lines.append("")
+    probes = bench.get("probes")
+    if probes:
+        lines += [f"Boundary probes ({probes['protocol']}):", "",
+                  "| probe | M×N×K | layout | path | p50 µs | GB/s | HBM frac |", "|---|---|---|---|---:|---:|---:|"]
+        for r in probes["boundary"]:
+            lines.append(f"| {r['id']} | {r['m']}×{r['n']}×{r['k']} | {r['layout']} | {r['path']}/{r['split']} | "
+                         f"{r['p50_us']:.2f} | {_fmt(r['gbs'], '.0f')} | {_fmt(r['frac'], '.3f')} |")
+        lines += ["", "| split probe | path | p50 µs | GB/s | HBM frac | FP32 partials |",
+                  "|---|---|---:|---:|---:|---:|"]
+        for r in probes["split"]:
+            lines.append(f"| M={r['m']} S={r['split']} | {r['path']}/{r['reported_split']} | {r['p50_us']:.2f} | "
+                         f"{r['gbs']:.0f} | {r['frac']:.3f} | {r['partial_bytes'] / 2**10:.0f} KiB |")
         lines.append("")
     e2e, cpu = bench.get("e2e"), bench.get("cpu_baseline")
     if e2e:

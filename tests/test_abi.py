@@ -103,7 +103,8 @@ def test_plan_boundaries():
 def test_plan_forced_split(m, split):
     path, s = plan(m, 4096, 4096, split=split)
     assert s == split
-    assert path == ("gemv_m1" if m == 1 else "tc_splitk")
+    # M = 1: the GEMV splits in two; larger forced splits use the tcgen05 kernel.
+    assert path == ("gemv_m1" if m == 1 and split == 2 else "tc_splitk")
 
 
 def test_plan_split_clamped_to_k_blocks():

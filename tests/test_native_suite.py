@@ -131,8 +131,18 @@ def test_report_of_bench_line():
                              "gbs": 4041.0, "cublas_fused_p50_us": 25.0}],
              "e2e": {"value": 675.5, "unit": "us", "h2d_bytes_per_step": 10, "d2h_bytes_per_step": 2},
              "cpu_baseline": {"value": 3201.8, "unit": "us", "cores": 16, "kind": "port", "sample": "s"},
-             "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}}
+             "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []},
+             "probes": {"protocol": "p",
+                        "boundary": [{"id": "zero-m", "m": 0, "n": 4096, "k": 4096, "layout": "w_nk", "path": "empty",
+                                      "split": 1, "p50_us": 0.0, "gbs": None, "frac": None},
+                                     {"id": "tail-k", "m": 32, "n": 4096, "k": 4090, "layout": "w_nk",
+                                      "path": "repacked", "split": 8, "p50_us": 25.0, "gbs": 1340.0, "frac": 0.2}],
+                        "split": [{"m": 8, "split": 4, "path": "tc_splitk", "reported_split": 4, "p50_us": 11.0,
+                                   "gbs": 3060.0, "frac": 0.468, "partial_bytes": 4 * 8 * 4096 * 4}]}}
     text = summarize.render(bench=bench)
+    assert "| zero-m | 0×4096×4096 | w_nk | empty/1 | 0.00 | — | — |" in text
+    assert "| tail-k | 32×4096×4090 | w_nk | repacked/8 | 25.00 | 1340 | 0.200 |" in text
+    assert "| M=8 S=4 | tc_splitk/4 | 11.00 | 3060 | 0.468 | 512 KiB |" in text
     assert "| 32 | tc_splitk/8 | 10.00 | 3400 | 0.520 | 9.80 | 20.00 |" in text
     assert "| 32×11008×4096 | tc_splitk/3 | 22.50 | 4041 | 25.00 |" in text
     assert "675.5 us" in text and "reasons none" in text
