@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the FP16 linear + bias + SiLU fragment on B200.
 
-Workload: y = SiLU(A @ W^T + b) and y = A @ W^T with
+Workload (the headline configs, N = K = 4096): y = SiLU(A @ W^T + b) and y = A @ W^T with
 A [M, 4096], W [4096, 4096] (K-contiguous), b [4096], seed-7 uniform
 [-0.5, 0.5) FP16 inputs, for M in {1, 8, 32, 128}.  One *step* runs the eight
 calls (four M values x {fused, plain}) in a freshly shuffled order, each call
@@ -75,7 +75,7 @@ def parse_args(argv=None):
     p.add_argument("--sweep", type=str, default=",".join(map(str, SWEEP_M)),
                    help="comma-separated M values of the step (default 1,8,32,128)")
     p.add_argument("--no-sharded-shapes", action="store_true",
-                   help="N > 1: skip the BASELINE sharded shapes (N = 8192 / 28672, K = 8192)")
+                   help="N > 1: skip the column-parallel shapes (N = 8192 / 28672, K = 8192)")
     return p.parse_args(argv)
 
 
@@ -321,7 +321,7 @@ def single_gpu(args, torch, dev) -> dict:
                     "plain": torch.empty((m, N_DIM), dtype=torch.float16, device=dev), "i": 0}
 
     # Gate before timing (the harness refuses to time wrong output): torch
-    # FP32 reference on the device, TF32 off, BASELINE tolerance.
+    # FP32 reference on the device, TF32 off, the uniform-corpus tolerance.
     paths = {}
     for m, st in state.items():
         kernels.triton_bias_silu_into(st["a"], st["w"][0].t(), st["bias"], st["fused"])
@@ -654,7 +654,7 @@ def multi_gpu(args, torch, dist, dev, world: int, rank: int) -> dict:
         kernels.triton_bias_silu_into(da, wi.t(), layer.bias, local)
         sharded.gather_columns(local, y_nccl, gathered=gathered)
 
-    # Correctness gate on every rank (torch FP32 reference, BASELINE tolerance).
+    # Correctness gate on every rank (torch FP32 reference, the uniform-corpus tolerance).
     y_fused = fused_step().clone()
     nccl_step()
     torch.cuda.synchronize()
@@ -735,12 +735,12 @@ def multi_gpu(args, torch, dist, dev, world: int, rank: int) -> dict:
             "h2d": ha.numel() * 2 + hw.numel() * 2 + hb.numel() * 2, "d2h": hy.numel() * 2}
 
 
-SHARDED_SHAPES = ((8192, 8192), (28672, 8192))  # (N, K) of BASELINE's column-parallel configs
+SHARDED_SHAPES = ((8192, 8192), (28672, 8192))  # (N, K) of the column-parallel configs
 SHARDED_M = (1, 32, 128, 4096)
 
 
 def sharded_shapes(args, torch, dist, dev, world: int, rank: int) -> list[dict]:
-    """BASELINE's column-parallel shapes, strong scaling: W [N, K] split along N
+    """The column-parallel shapes, strong scaling: W [N, K] split along N
     over the ranks, fused bias+SiLU, all-gather fused into the kernel.  Inputs
     are uniform [-0.5, 0.5) draws of the device generator seeded 7 (the full
     layer is generated identically on every rank and sliced).  Rank 0 also
@@ -869,7 +869,7 @@ def run_native(args) -> int:
                                          "bound at these sizes"}}
             if "sharded_shapes" in res:
                 line["sharded_shapes"] = {
-                    "workload": "BASELINE column-parallel configs: fused linear+bias+SiLU, W [N, K] split along N "
+                    "workload": "column-parallel configs: fused linear+bias+SiLU, W [N, K] split along N "
                                 "over the ranks (strong scaling), all-gather fused into the kernel; device-"
                                 "generator seed-7 uniform inputs; p50 of back-to-back calls, max over ranks; "
                                 "tensor_frac against bf16_tflops_sustained of MEASURED_PEAKS.json",

@@ -33,7 +33,7 @@ def stats(values: list[float]) -> dict:
 
 def torch_measure(functions: dict[str, Callable[[], object]], samples: int = 31, warmup: int = 20,
                   inner: int = 10, seed: int = 1729) -> dict:
-    """The reference's protocol; warmup defaults to the 20 BASELINE asks for."""
+    """The reference's protocol; warmup defaults to 20 calls, as the headline metric specifies."""
     import torch
     if samples < 3 or warmup < 0 or inner < 1:
         raise ValueError("invalid benchmark parameters")

@@ -34,7 +34,7 @@ import math
 
 import numpy as np
 
-# BASELINE gate for the seed-7 uniform corpus: abs <= 0.02 + 0.002 * |ref|.
+# Gate for the seed-7 uniform corpus: abs <= 0.02 + 0.002 * |ref|.
 UNIFORM_ATOL = 0.02
 UNIFORM_RTOL = 0.002
 # The reference corpus' own gates (manifests/workloads.json:6-7,

@@ -112,7 +112,7 @@ def main() -> int:
     arrays["kat/expected"] = q.reference(a, b).numpy()
     meta["cases"]["kat"] = {"m": 2, "n": 2, "k": 2, "full": True}
 
-    # Seed-7 uniform contract, reference oracle on our inputs.
+    # Seed-7 uniform contract (the headline configs), reference oracle on our inputs.
     for m in (1, 8, 32, 128):
         n = k = 4096
         a, w, bias = uniform_inputs(m, n, k)

@@ -145,7 +145,7 @@ def test_crosscheck_rejects_corrupt_reference():
 
 
 def test_uniform_gate_bounds():
-    """The BASELINE gate: pass at the bound, fail just beyond it."""
+    """The uniform-corpus gate: pass at the bound, fail just beyond it."""
     expected = np.array([[10.0, -3.0]])
     ok = expected + np.array([[0.02 + 0.002 * 10.0, -(0.02 + 0.002 * 3.0)]]) * 0.999
     oracle.compare(ok, expected, oracle.UNIFORM_ATOL, oracle.UNIFORM_RTOL)

@@ -52,7 +52,7 @@ def clean_error_word(cuda_device):
     assert native.device_error(clear=True) == 0, "a bounded in-kernel wait expired"
 
 
-# ------------------------------------------------------------------ BASELINE sweep
+# ------------------------------------------------------------------ headline sweep (M = 1..128, N = K = 4096)
 
 @pytest.mark.parametrize("m", [1, 8, 32, 128])
 def test_uniform_sweep_fused(cuda_device, golden, m):
