@@ -20,7 +20,7 @@ LIBRARY_PATH = Path(__file__).resolve().parent / "libglq.so"
 DTYPE_F16, DTYPE_BF16 = 0, 1
 EPILOGUE_NONE, EPILOGUE_BIAS, EPILOGUE_BIAS_SILU = 0, 1, 2
 PATHS = ("empty", "zero_k", "gemv_m1", "tc_tcgen05", "tc_splitk", "tail", "strided", "unaligned", "tc_kn",
-         "repacked")
+         "repacked", "tc_ldg")
 STATUS_OK = 0
 STATUS_NAMES = ("ok", "invalid_argument", "shape", "split", "workspace", "output_layout", "cuda",
                 "device", "device_timeout", "scratch")

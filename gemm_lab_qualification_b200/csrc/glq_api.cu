@@ -149,6 +149,10 @@ OperandLayout classify(const Problem& p) {
   return L;
 }
 
+bool ldg_w(const Problem& p, const OperandLayout& L) {
+  return L.w_kmajor && !L.w_ok && L.a_ok && !p.require_tc && !small_problem(p.m, p.n, p.k);
+}
+
 bool repack_plan(const Problem& p, RepackPlan* r) {
   *r = RepackPlan();
   // Small problems run the small kernel on the operands as they are.
@@ -207,6 +211,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->tile_n = 128;
   c->stages = 0;
   c->w_mn = 0;
+  c->w_ldg = 0;
   if (p.m == 0 || p.n == 0) {
     c->path = GLQ_PATH_EMPTY;
     c->kernel = kKernelNone;
@@ -223,17 +228,22 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
     c->kernel = small_problem(p.m, p.n, p.k) ? kKernelSmall : kKernelGeneric;
     return GLQ_OK;
   }
-  if (!L.w_ok || !L.a_ok) {
+  // K-major W rows that TMA cannot address (odd K, an odd row pitch or
+  // base), with an addressable A: the tcgen05 kernel loads W by the SM
+  // (4x the generic kernel; a call with a repack workspace copies W instead).
+  const bool ldg = ldg_w(p, L);
+  if ((!L.w_ok || !L.a_ok) && !ldg) {
     c->path = GLQ_PATH_UNALIGNED;
     c->kernel = small_problem(p.m, p.n, p.k) ? kKernelSmall : kKernelGeneric;
     return GLQ_OK;
   }
   c->w_mn = L.w_mnmajor ? 1 : 0;
+  c->w_ldg = ldg ? 1 : 0;
   // M = 1 runs a GEMV, except for a forced split of 4 or more: the register
   // GEMV then holds one or two rows per block and every block re-stages all
   // of A (19 us at S = 8 vs 9.9 us for the tcgen05 split, which writes the
   // same [S, 1, N] FP32 partials).
-  if (p.m == 1 && L.w_kmajor && !p.require_tc && split_k < 4) {
+  if (p.m == 1 && L.w_kmajor && !p.require_tc && split_k < 4 && !ldg) {
     const int sms = sm_count > 0 ? sm_count : 148;
     // The ring GEMV holds a whole SM per CTA, so with static weights (where a
     // call's weight stream should start while its predecessor drains) the
@@ -246,7 +256,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   }
   c->kernel = kKernelTc;
   c->tile_t = tc_token_tile(p.m);
-  c->tile_n = tc_tile_rows(p.m, p.n);
+  c->tile_n = ldg ? 128 : tc_tile_rows(p.m, p.n);  // the SM-loaded W fills 128-row tiles
   const int64_t k_blocks = tc_k_blocks(p.k);
   const int64_t tiles = ((p.n + c->tile_n - 1) / c->tile_n) * ((p.m + c->tile_t - 1) / c->tile_t);
   const int sms = sm_count > 0 ? sm_count : 148;
@@ -266,11 +276,13 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   // Prefill-sized problems (256-token tiles, no split) with at least one
   // wave of 256 x 256 output tiles: two M = 128 MMAs per K step share the
   // token tile, doubling the FLOPs per staged byte.
-  if (c->split == 1 && c->tile_t == 256 &&
+  if (c->split == 1 && c->tile_t == 256 && !ldg &&
       ((p.n + 255) / 256) * ((p.m + 255) / 256) >= static_cast<int64_t>(sms)) {
     c->tile_n = 256;
   }
-  if (p.n % 128 != 0 || p.k % 64 != 0) {
+  if (ldg) {
+    c->path = GLQ_PATH_TC_LDG;
+  } else if (p.n % 128 != 0 || p.k % 64 != 0) {
     c->path = GLQ_PATH_TAIL;
   } else if (c->w_mn) {
     c->path = GLQ_PATH_TC_KN;
@@ -334,6 +346,9 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
     if (M > 1 && y_row_stride < N) return GLQ_ERR_OUTPUT_LAYOUT;
     if (epilogue != GLQ_EPILOGUE_NONE && bias == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
     if (K > 0 && (A == nullptr || B == nullptr)) return GLQ_ERR_INVALID_ARGUMENT;
+    // 16-bit elements: every element pointer is 2-byte aligned.
+    auto odd = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 1u) != 0; };
+    if (odd(Y) || (bias != nullptr && odd(bias)) || (K > 0 && (odd(A) || odd(B)))) return GLQ_ERR_INVALID_ARGUMENT;
   }
   Problem p = {};
   p.dtype = dtype;
@@ -367,10 +382,11 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Strided or unaligned operands with a workspace that holds their aligned
   // copies: repack, then plan the copies (tcgen05 / GEMV instead of the
-  // generic kernel).
+  // generic kernel, or of the SM-loaded W, which streams W at about half the
+  // copy-then-TMA rate: 51 vs 25 us at 32 x 4096 x 4090).
   glq::RepackPlan rp;
-  const bool repack = c.kernel == glq::kKernelGeneric && workspace != nullptr && glq::aligned16(workspace) &&
-                      glq::repack_plan(p, &rp) && workspace_bytes >= rp.bytes();
+  const bool repack = (c.kernel == glq::kKernelGeneric || c.w_ldg) && workspace != nullptr &&
+                      glq::aligned16(workspace) && glq::repack_plan(p, &rp) && workspace_bytes >= rp.bytes();
   if (repack) {
     if (glq::launch_repacks(p, rp, workspace, dev->sm_count, s) != cudaSuccess) {
       cudaGetLastError();
@@ -380,10 +396,12 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
     v = glq::plan_problem(p, split_k, dev->sm_count, &c);
     if (v != GLQ_OK) return v;
   } else if (workspace != nullptr && c.split > 1) {
+    // The FP32 partials are stored as floats: a 4-byte aligned buffer.
     const size_t need = static_cast<size_t>(c.split) * static_cast<size_t>(M) * static_cast<size_t>(N) * sizeof(float);
-    if (workspace_bytes < need) return GLQ_ERR_WORKSPACE;
+    if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) return GLQ_ERR_WORKSPACE;
     p.partial = static_cast<float*>(workspace);
   }
+  p.w_ldg = c.w_ldg;
   cudaError_t e = cudaSuccess;
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;
@@ -576,6 +594,7 @@ const char* glq_path_name(int path) {
     case GLQ_PATH_UNALIGNED: return "unaligned";
     case GLQ_PATH_TC_KN: return "tc_kn";
     case GLQ_PATH_REPACKED: return "repacked";
+    case GLQ_PATH_TC_LDG: return "tc_ldg";
     default: return "unknown";
   }
 }
@@ -586,7 +605,7 @@ const char* glq_status_string(int status) {
     case GLQ_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer, dtype or epilogue)";
     case GLQ_ERR_SHAPE: return "invalid shape or stride";
     case GLQ_ERR_SPLIT: return "split_k must be in 0..8";
-    case GLQ_ERR_WORKSPACE: return "workspace smaller than split * M * N * 4 bytes";
+    case GLQ_ERR_WORKSPACE: return "workspace smaller than split * M * N * 4 bytes, or not 4-byte aligned";
     case GLQ_ERR_OUTPUT_LAYOUT: return "output row stride smaller than N";
     case GLQ_ERR_CUDA: return "CUDA runtime or driver call failed";
     case GLQ_ERR_DEVICE: return "no usable device: the kernels need a compute capability 10.0 (sm_100a) GPU";

@@ -41,6 +41,7 @@ struct Problem {
   float* partial;  // optional [split, m, n] FP32 split partials
   unsigned int flags;  // glq_flags
   int require_tc;      // 1: the tcgen05 kernel or an error (fused gather)
+  int w_ldg;           // 1: K-major W rows not TMA-addressable, loaded by the SM (tc kernel)
 };
 
 // Fused all-gather of a column-parallel layer (glq_linear_gather): output
@@ -71,6 +72,9 @@ struct RepackPlan {
   size_t a_bytes = 0, w_bytes = 0;
   size_t bytes() const { return a_bytes + w_bytes; }
 };
+// True when W is K-major with rows TMA cannot address and A is addressable:
+// the tcgen05 kernel then loads W by the SM (path tc_ldg).
+bool ldg_w(const Problem& p, const OperandLayout& L);
 // False when every operand is already TMA-addressable (or nothing to do).
 bool repack_plan(const Problem& p, RepackPlan* r);
 // The same problem reading the copies in `workspace`.
@@ -86,6 +90,7 @@ struct Choice {
   int tile_n;   // W rows per CTA of the tcgen05 kernel (128 or 256)
   int stages;   // TMA ring depth of the tcgen05 kernel (5: two CTAs per SM)
   int w_mn;     // 1: W = B^T is N-contiguous (B = [K, N]); MN-major W tiles
+  int w_ldg;    // 1: K-major W rows TMA cannot address, loaded by the SM (path tc_ldg)
 };
 
 enum Kernel : int {

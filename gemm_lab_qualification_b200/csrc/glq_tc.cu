@@ -157,12 +157,134 @@ struct TcArgs {
   int recv_overlaps;        // 1: the receive buffer reuses the drained pipeline stages
   uint32_t barrier_offset;  // mbarriers, bytes from the aligned base
   unsigned int flags;       // glq_flags
+  // LDG kernels: W [N, K] K-contiguous rows that TMA cannot address (row
+  // pitch or base not 16-byte aligned), loaded by the SM.
+  const void* w_ptr;
+  long long w_pitch_bytes;
 };
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER>
-__global__ void __launch_bounds__(kThreads, 1)
+// W rows loaded by the SM instead of TMA: warps 2..5 fill each stage.
+constexpr int kLdgWarps = 4;
+constexpr int kLdgThreads = kLdgWarps * 32;
+
+// ---- W producer for rows that TMA cannot address (LDG kernels).
+//
+// Thread t (0..127, warps 2..5) owns 16-byte chunk c = t % 8 of rows
+// r = t / 8 + 16 j (j = 0..7) of each 128-row x 64-K stage, so a warp covers
+// four rows of 128 contiguous bytes per step.  Chunk c of a row starts at
+// byte offset `shift` (the same for every chunk of the row) inside the
+// aligned granule G + 16 c; its bytes are that granule and the next one,
+// which is the neighbouring lane's granule (shuffle) except for c = 7, which
+// loads it.  A granule is read only if it holds bytes of the row (the first
+// always does unless the row is past N; the others are skipped past the
+// row's end), and an aligned 16-byte granule never crosses a page.  Columns
+// k >= K and rows n >= N are written as zero, as TMA's out-of-bounds fill
+// would.  Each chunk goes to its 128-byte-swizzle position (chunk c of row r
+// at r * 128 + ((c ^ (r % 8)) * 16)), the layout the K-major UMMA descriptor
+// reads; the writes are made visible to the tensor core with
+// fence.proxy.async before every thread's arrival on the stage's full
+// barrier.  All loads of a half stage are issued before any is used.
+template <typename T, int BT, int TN, int STAGES, typename FullBar, typename EmptyBar, typename Raise>
+__device__ __forceinline__ void ldg_fill_w(const TcArgs& args, uint8_t* smem, int kb_begin, int nkb, int tile_n,
+                                           FullBar full_bar, EmptyBar empty_bar, const volatile int* abort_flag,
+                                           Raise raise) {
+  using Cfg = TcConfig<BT, TN, STAGES>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kRowsPerPass = kLdgThreads / 8;  // 16
+  constexpr int kPasses = TN / kRowsPerPass;      // 8
+  constexpr int kBatch = 4;                       // passes whose loads are in flight together
+  const int t = static_cast<int>(threadIdx.x) - 64;
+  const int lane = t & 31;
+  const int c = t & 7;
+  const uintptr_t wbase = reinterpret_cast<uintptr_t>(args.w_ptr);
+  const long long row_bytes = static_cast<long long>(args.k) * 2;
+  for (int i = 0; i < nkb; ++i) {
+    const int stage = i % kStages;
+    if (i >= kStages) {
+      bool ok = true;
+      if (lane == 0) {
+        ok = ptx::mbar_wait_bounded(empty_bar(stage), static_cast<uint32_t>(i / kStages - 1) & 1u, abort_flag,
+                                    kWaitBudgetNs);
+      }
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+        if (lane == 0) raise(kErrTimeoutProducer);
+        return;
+      }
+    }
+    const long long k0 = static_cast<long long>(kb_begin + i) * kTileK;
+    uint8_t* const w_stage = smem + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
+#pragma unroll
+    for (int b = 0; b < kPasses; b += kBatch) {
+      uint4 lo[kBatch], hi[kBatch];
+      unsigned shift[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int r = t / 8 + kRowsPerPass * (b + j);
+        const long long n = static_cast<long long>(tile_n) * TN + r;
+        lo[j] = make_uint4(0u, 0u, 0u, 0u);
+        hi[j] = make_uint4(0u, 0u, 0u, 0u);
+        shift[j] = 0;
+        if (n < args.n) {
+          const uintptr_t row_begin = wbase + static_cast<uintptr_t>(n * args.w_pitch_bytes);
+          const uintptr_t row_end = row_begin + static_cast<uintptr_t>(row_bytes);
+          const uintptr_t first = row_begin + static_cast<uintptr_t>(k0 * 2);
+          const uintptr_t g = (first & ~static_cast<uintptr_t>(15)) + 16u * static_cast<uintptr_t>(c);
+          shift[j] = static_cast<unsigned>(first & 15u);
+          if (g < row_end) lo[j] = __ldg(reinterpret_cast<const uint4*>(g));
+          if (c == 7 && shift[j] != 0 && g + 16 < row_end) hi[j] = __ldg(reinterpret_cast<const uint4*>(g + 16));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const uint32_t nx = __shfl_down_sync(0xffffffffu, lo[j].x, 1);
+        const uint32_t ny = __shfl_down_sync(0xffffffffu, lo[j].y, 1);
+        const uint32_t nz = __shfl_down_sync(0xffffffffu, lo[j].z, 1);
+        const uint32_t nw = __shfl_down_sync(0xffffffffu, lo[j].w, 1);
+        if (c != 7) hi[j] = make_uint4(nx, ny, nz, nw);
+        const int r = t / 8 + kRowsPerPass * (b + j);
+        const long long n = static_cast<long long>(tile_n) * TN + r;
+        const long long valid = static_cast<long long>(args.k) - (k0 + 8 * c);
+        uint32_t out[4] = {0u, 0u, 0u, 0u};
+        if (n < args.n && valid > 0) {
+          const uint32_t w[8] = {lo[j].x, lo[j].y, lo[j].z, lo[j].w, hi[j].x, hi[j].y, hi[j].z, hi[j].w};
+          const unsigned q = shift[j] >> 2;
+          const unsigned bits = (shift[j] & 3u) * 8u;
+          uint32_t pick[5];
+#pragma unroll
+          for (int e = 0; e < 5; ++e) {
+            const uint32_t x0 = w[e], x1 = w[e + 1 < 8 ? e + 1 : 7], x2 = w[e + 2 < 8 ? e + 2 : 7],
+                           x3 = w[e + 3 < 8 ? e + 3 : 7];
+            pick[e] = q == 0 ? x0 : q == 1 ? x1 : q == 2 ? x2 : x3;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) out[e] = __funnelshift_r(pick[e], pick[e + 1], bits);
+          if (valid < 8) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (2 * e >= valid) {
+                out[e] = 0u;
+              } else if (2 * e + 1 >= valid) {
+                out[e] &= 0xFFFFu;
+              }
+            }
+          }
+        }
+        *reinterpret_cast<uint4*>(w_stage + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+      }
+    }
+    ptx::fence_proxy_async_smem();
+    ptx::mbar_arrive(full_bar(stage));
+  }
+}
+
+// LDG: the W tiles are written into the swizzled stages by warps 2..5 from
+// plain 16-byte loads (K-major W, 128-row tiles, no gather); two CTAs per SM
+// must still fit, so these instantiations are capped at 128 registers.
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, bool LDG = false>
+__global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_a, const TcArgs args) {
+  static_assert(!LDG || (!WMN && !GATHER && TN == 128), "SM-loaded W: K-major 128-row tiles only");
   using Cfg = TcConfig<BT, TN, STAGES>;
   constexpr uint32_t kWTileBytes = Cfg::kWTileBytes;
   constexpr int kStages = Cfg::kStages;
@@ -233,12 +355,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tma_load_2d(a_dst, &tmap_a, (kb_begin + i) * kTileK, tile_t * BT, full_bar(stage), pol_a);
   };
   auto issue = [&](int i) {
-    issue_w(i);
+    if constexpr (LDG) {
+      // The W half of the stage arrives through the producer warps' arrivals.
+      ptx::mbar_arrive_expect_tx(full_bar(i % kStages), Cfg::kATileBytes);
+    } else {
+      issue_w(i);
+    }
     issue_a(i);
   };
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
-      ptx::mbar_init(full_bar(i), 1);
+      // LDG: thread 0 (A, expect_tx) plus every W producer thread arrives.
+      ptx::mbar_init(full_bar(i), LDG ? 1 + kLdgThreads : 1);
       ptx::mbar_init(empty_bar(i), 1);
     }
     ptx::mbar_init(done_bar, 1);
@@ -261,13 +389,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // caller declared the weights static) is read only after the dependency
     // wait.
     const int first = nkb < kStages ? nkb : kStages;
-    const bool static_w = (args.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
+    const bool static_w = !LDG && (args.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
     if (static_w) {
       for (int i = 0; i < first; ++i) issue_w(i);
     }
     ptx::grid_dependency_wait();
     for (; issued < first; ++issued) {
-      if (!static_w) issue_w(issued);
+      if constexpr (LDG) {
+        ptx::mbar_arrive_expect_tx(full_bar(issued), Cfg::kATileBytes);
+      } else {
+        if (!static_w) issue_w(issued);
+      }
       issue_a(issued);
     }
     *issued_slot = issued;
@@ -307,9 +439,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the wait during the main loop; when the buffer reuses the pipeline it is
   // armed only after the main loop.
   const bool recv_dedicated = split > 1 && !args.recv_overlaps;
+  // W producer warps (LDG) wait after their loop instead.
+  const bool ldg_producer = LDG && warp >= 2 && warp < 2 + kLdgWarps;
   if (recv_dedicated) {
     ptx::cluster_arrive_relaxed();
-    if (warp >= 2) ptx::cluster_wait();
+    if (warp >= 2 && !ldg_producer) ptx::cluster_wait();
   }
 
   if (warp == 0) {
@@ -359,9 +493,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::tc_commit(done_bar);
     }
+  } else if (ldg_producer) {
+    if constexpr (LDG) ldg_fill_w<T, BT, TN, STAGES>(args, smem, kb_begin, nkb, tile_n, full_bar, empty_bar,
+                                                      abort_flag, raise);
   }
   __syncwarp();
-  if (recv_dedicated && warp < 2) ptx::cluster_wait();
+  if (recv_dedicated && (warp < 2 || ldg_producer)) ptx::cluster_wait();
 
   // ---- Epilogue: 8 warps (rows and chunks as assigned above).
   if (!ptx::mbar_wait_bounded(done_bar, 0u, abort_flag, kWaitBudgetNs)) {
@@ -678,15 +815,18 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, bool LDG = false>
 cudaError_t set_attr() {
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER>,
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, LDG>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
 }
 
 template <typename T, int BT, int TN, int STAGES>
 cudaError_t set_attrs() {
   cudaError_t e;
+  if constexpr (TN == 128) {
+    if ((e = set_attr<T, BT, TN, STAGES, false, false, true>()) != cudaSuccess) return e;
+  }
   if ((e = set_attr<T, BT, TN, STAGES, false, false>()) != cudaSuccess) return e;
   if ((e = set_attr<T, BT, TN, STAGES, true, false>()) != cudaSuccess) return e;
   if ((e = set_attr<T, BT, TN, STAGES, false, true>()) != cudaSuccess) return e;
@@ -708,13 +848,15 @@ cudaError_t set_attrs_all() {
   return set_attrs<T, 256, 128, 4>();
 }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, bool LDG = false>
 cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
   CUtensorMap tmap_w, tmap_a;
   const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
-  bool ok;
-  if constexpr (WMN) {
+  bool ok = true;
+  if constexpr (LDG) {
+    // W is read by the SM: no W tensor map (the kernel gets A's as a stand-in).
+  } else if constexpr (WMN) {
     // B = [K, N]: rows k (pitch b_ks), N contiguous; boxes 64(n) x 64(k).
     ok = encode_2d(&tmap_w, Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
   } else {
@@ -726,6 +868,7 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   if (!ok || !encode_2d(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, kTileK, BT)) {
     return cudaErrorInvalidValue;
   }
+  if constexpr (LDG) tmap_w = tmap_a;
   using Cfg = TcConfig<BT, TN, STAGES>;
   TcArgs args;
   args.m = static_cast<int>(p.m);
@@ -757,6 +900,8 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   args.partial = p.partial;
   args.err = err;
   args.flags = p.flags;
+  args.w_ptr = LDG ? p.b : nullptr;
+  args.w_pitch_bytes = LDG && p.n > 1 ? p.b_ns * esz : 0;
   // Shared memory: [pipeline stages][split-K receive buffer][mbarriers].
   // The receive buffer ((split - 1) remote sources x TN rows x owned groups
   // x 16 B) gets its own
@@ -811,7 +956,29 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER>, tmap_w, tmap_a, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, LDG>, tmap_w, tmap_a, args);
+}
+
+// K-major W rows that TMA cannot address: the LDG kernels (128-row tiles).
+template <typename T>
+cudaError_t launch_ldg(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
+                       cudaStream_t s) {
+  if (tile_n != 128) return cudaErrorInvalidValue;
+  if (stages == kPairStages) {
+    switch (tile_t) {
+      case 16: return launch_typed<T, 16, 128, kPairStages, false, false, true>(p, split, nullptr, err, s);
+      case 32: return launch_typed<T, 32, 128, kPairStages, false, false, true>(p, split, nullptr, err, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  switch (tile_t) {
+    case 16: return launch_typed<T, 16, 128, 8, false, false, true>(p, split, nullptr, err, s);
+    case 32: return launch_typed<T, 32, 128, 8, false, false, true>(p, split, nullptr, err, s);
+    case 64: return launch_typed<T, 64, 128, 8, false, false, true>(p, split, nullptr, err, s);
+    case 128: return launch_typed<T, 128, 128, 6, false, false, true>(p, split, nullptr, err, s);
+    case 256: return launch_typed<T, 256, 128, 4, false, false, true>(p, split, nullptr, err, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <typename T, bool WMN, bool GATHER>
@@ -852,6 +1019,11 @@ cudaError_t tc_prepare_device() {
 
 cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
                       const Gather* g, unsigned int* err, cudaStream_t s) {
+  if (p.w_ldg) {
+    if (g != nullptr || w_mn) return cudaErrorInvalidValue;
+    return p.dtype == GLQ_DTYPE_BF16 ? launch_ldg<__nv_bfloat16>(p, split, tile_t, tile_n, stages, err, s)
+                                     : launch_ldg<__half>(p, split, tile_t, tile_n, stages, err, s);
+  }
   if (g != nullptr) {
     if (p.dtype == GLQ_DTYPE_BF16) {
       return w_mn ? launch_bt<__nv_bfloat16, true, true>(p, split, tile_t, tile_n, stages, g, err, s)

@@ -76,7 +76,11 @@ enum glq_path {
   GLQ_PATH_REPACKED = 9,  /* strided or unaligned operands copied into the
                              caller's workspace with 16-B aligned rows, then
                              the tcgen05 or GEMV kernel on the copies */
-  GLQ_PATH_COUNT = 10
+  GLQ_PATH_TC_LDG = 10,    /* no repack workspace, K-contiguous W rows not
+                             16-B aligned (odd K, pitch or base), A
+                             addressable: tcgen05 GEMM whose W stages the SM
+                             fills with plain loads */
+  GLQ_PATH_COUNT = 11
 };
 
 enum glq_status {
@@ -84,7 +88,7 @@ enum glq_status {
   GLQ_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad dtype/epilogue value */
   GLQ_ERR_SHAPE = 2,            /* negative or too large M/N/K, bad strides */
   GLQ_ERR_SPLIT = 3,            /* split_k outside 0..GLQ_MAX_SPLIT */
-  GLQ_ERR_WORKSPACE = 4,        /* workspace given but smaller than needed */
+  GLQ_ERR_WORKSPACE = 4,        /* partial-sum workspace smaller than needed or not 4-B aligned */
   GLQ_ERR_OUTPUT_LAYOUT = 5,    /* y_row_stride < N */
   GLQ_ERR_CUDA = 6,             /* CUDA runtime or driver call failed */
   GLQ_ERR_DEVICE = 7,           /* no device, or not a compute 10.0 GPU */
@@ -118,13 +122,15 @@ enum glq_flags {
  *   B[k, n]   at B + k * b_k_stride   + n * b_n_stride          (elements)
  *   bias[n]   at bias + n (contiguous; required unless epilogue NONE)
  *   Y[m, n]   at Y + m * y_row_stride + n                        (unit column stride)
+ *   A, B, bias and Y are 2-byte aligned (GLQ_ERR_INVALID_ARGUMENT otherwise).
  *
  * split_k: 0 = library choice; 1..GLQ_MAX_SPLIT = split the K reduction into
  *   that many contiguous ranges merged in-kernel in split order (the merge is
  *   deterministic).  A path that cannot split reports split 1.
  * workspace: optional (may be NULL).  When non-NULL it receives the FP32
  *   per-split partial sums in the lab's [split, M, N] layout
- *   (kernels.py:431-439), and must hold glq_workspace_bytes() bytes.  The
+ *   (kernels.py:431-439), and must hold glq_workspace_bytes() bytes and be
+ *   4-byte aligned (GLQ_ERR_WORKSPACE otherwise).  The
  *   merge itself never needs it.  For operands the TMA kernels cannot
  *   address, a workspace of glq_linear_workspace_bytes() bytes instead
  *   holds their aligned copies (GLQ_PATH_REPACKED).
@@ -207,8 +213,10 @@ size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k);
  * the workspace with 16-byte aligned rows, and the call then runs the
  * tcgen05 or GEMV kernel on the copies (path GLQ_PATH_REPACKED).  0 when
  * the operands are addressable as they are.  Given less, such a call runs
- * the generic kernel (GLQ_PATH_STRIDED / GLQ_PATH_UNALIGNED), as it does
- * when the workspace is not 16-byte aligned.  When the
+ * the generic kernel (GLQ_PATH_STRIDED / GLQ_PATH_UNALIGNED) or, for a
+ * K-contiguous W with an addressable A, the tcgen05 kernel with W loaded by
+ * the SM (GLQ_PATH_TC_LDG), as it does when the workspace is not 16-byte
+ * aligned.  When the
  * workspace serves a repack it holds no split partials.  Pure host function.
  * No counterpart in the reference: the lab's Triton kernel reads any
  * contiguous layout through masked loads (kernels.py:103-129) and sends

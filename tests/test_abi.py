@@ -95,7 +95,13 @@ def test_plan_boundaries():
     assert plan(32, 4096, 4096, b_strides=(2, 8192))[0] == "strided"
     # base one element off 16-byte alignment.
     assert plan(32, 4096, 4096, a_ptr=2)[0] == "unaligned"
-    assert plan(1, 4096, 4096, b_ptr=2)[0] == "unaligned"
+    # K-contiguous W rows that TMA cannot address with an addressable A: the
+    # tcgen05 kernel loads W by the SM (odd base, pitch or K) when the call
+    # has no repack workspace (what glq_plan plans).
+    assert plan(1, 4096, 4096, b_ptr=2)[0] == "tc_ldg"
+    assert plan(32, 4096, 4090, a_strides=(4096, 1)) == ("tc_ldg", 8)
+    assert plan(32, 4096, 4096, b_strides=(1, 4100)) == ("tc_ldg", 8)
+    assert plan(128, 4096, 4096, b_strides=(1, 4097)) == ("tc_ldg", 4)
 
 
 @pytest.mark.parametrize("m", [1, 8, 32])
@@ -189,7 +195,8 @@ def test_linear_workspace_bytes():
     # tail) run the small kernel on the operands as they are: no copy.
     assert repack_bytes(17, 257, 131, b_strides=(257, 1)) == 0
     assert repack_bytes(1, 4096, 1023) == 0
-    assert repack_bytes(1, 4096, 1025) > 0
+    assert repack_bytes(1, 4096, 1025) == padded(4096, 1025)
+    assert repack_bytes(1, 4093, 4096, b_strides=(4093, 1)) == padded(4096, 4093)
     # nothing to compute, or invalid arguments.
     assert repack_bytes(0, 4096, 4090) == 0
     assert repack_bytes(32, 4096, 0) == 0
@@ -253,6 +260,10 @@ def test_linear_validation_precedes_device_use():
                              None, None) == 1
     # bias+SiLU without a bias pointer
     assert lib.glq_linear(0, 16, 1, 1, 16, 1, 1, None, 2, 16, 1, 1, 1, 1, 0, None, 0, None, None, None) == 1
+    # 16-bit element pointers at odd addresses (A, B, bias, Y in turn)
+    for a_ptr, b_ptr, bias_ptr, y_ptr in ((17, 16, 16, 16), (16, 17, 16, 16), (16, 16, 17, 16), (16, 16, 16, 17)):
+        assert lib.glq_linear(0, a_ptr, 8, 1, b_ptr, 1, 8, bias_ptr, 2, y_ptr, 8, 2, 8, 8, 0, None, 0, None,
+                              None, None) == 1
     # empty problems succeed without touching a device and report "empty"
     assert lib.glq_linear(0, None, 0, 1, None, 1, 0, None, 0, None, 0, 0, 8, 8, 0, None, 0, None,
                           ctypes.byref(path), ctypes.byref(split)) == 0

@@ -230,9 +230,10 @@ def aligned_copy(x: torch.Tensor, device) -> torch.Tensor:
 # B[K, N] row-major, "w_strided" = W[N, K].T with neither stride unit.
 REPACK_CASES = [
     ("k4090", 32, 4096, 4090, "contiguous", "w_nk"),
-    ("k131-wide", 64, 2055, 131, "contiguous", "b_kn"),
     ("m1-k4090", 1, 4096, 4090, "contiguous", "w_nk"),
+    ("k131-wide", 64, 2055, 131, "contiguous", "b_kn"),
     ("n4093-b_kn", 32, 4093, 4096, "contiguous", "b_kn"),
+    ("m1-n4093-b_kn", 1, 4093, 4096, "contiguous", "b_kn"),
     ("a-offset", 32, 4096, 4096, "offset", "w_nk"),
     ("a-transposed", 32, 4096, 4096, "transposed", "w_nk"),
     ("w-strided", 8, 2048, 520, "contiguous", "w_strided"),
@@ -259,7 +260,9 @@ def test_repacked_matches_aligned_copy(cuda_device, case, dtype):
     """Strided or unaligned operands with a workspace: the repack kernel's
     aligned copies go through the same tcgen05 / GEMV plan as operands that
     were aligned to begin with, so the bits equal that call's; without a
-    workspace the generic kernel runs.  Both pass the oracle gate."""
+    workspace the generic kernel runs (or, when only a K-contiguous W is
+    off, the tcgen05 kernel with W loaded by the SM).  Both pass the oracle
+    gate."""
     _, m, n, k, _, b_layout = case
     a, w, bias, da, b = layout_operands(case, dtype, cuda_device)
     b_al = aligned_copy(w.t().contiguous(), cuda_device) if b_layout == "b_kn" else aligned_copy(w, cuda_device).t()
@@ -275,8 +278,9 @@ def test_repacked_matches_aligned_copy(cuda_device, case, dtype):
     epi = native.EPILOGUE_BIAS_SILU
     out_generic = torch.empty((m, n), dtype=dtype, device=cuda_device)
     out_rep, out_al = torch.empty_like(out_generic), torch.empty_like(out_generic)
-    path_g, _ = native.linear(da, b, out_generic, db, epi)
-    assert path_g in ("unaligned", "strided")
+    path_g, split_g = native.linear(da, b, out_generic, db, epi)
+    # no workspace: the generic kernel, or the SM-loaded W when only W is off
+    assert path_g in ("unaligned", "strided", "tc_ldg")
     path_r, split_r = native.linear(da, b, out_rep, db, epi, workspace=ws)
     assert path_r == "repacked"
     path_a, split_a = native.linear(a_al, b_al, out_al, db, epi)
@@ -287,9 +291,16 @@ def test_repacked_matches_aligned_copy(cuda_device, case, dtype):
     expected = oracle.linear_reference(a, w, bias, silu=True, samples=8)
     oracle.compare(host(out_rep), expected, atol, rtol)
     oracle.compare(host(out_generic), expected, atol, rtol)
-    # A workspace that is too small (or misaligned) leaves the generic kernel.
+    # A workspace that is too small or misaligned holds no copies: the call
+    # takes its no-workspace path.  If that path splits K, the workspace is
+    # its FP32 partial buffer, which must be 4-byte aligned.
     assert native.linear(da, b, out_rep, db, epi, workspace=store[:need - 1])[0] == path_g
-    assert native.linear(da, b, out_rep, db, epi, workspace=store[1:need + 1])[0] == path_g
+    if split_g == 1:
+        assert native.linear(da, b, out_rep, db, epi, workspace=store[1:need + 1])[0] == path_g
+    else:
+        with pytest.raises(native.GlqError) as e:
+            native.linear(da, b, out_rep, db, epi, workspace=store[1:need + 1])
+        assert native.STATUS_NAMES[e.value.status] == "workspace"
 
 
 # Small problems (<= 2^22 multiply-adds) in layouts the TMA kernels cannot
@@ -328,6 +339,57 @@ def test_small_kernel(cuda_device, case, dtype):
     plain = torch.empty_like(out)
     native.linear(da, b, plain, None, native.EPILOGUE_NONE)
     oracle.compare(host(plain), oracle.linear_reference(a, w, samples=8), atol, rtol)
+
+
+# Without a workspace: K-contiguous W rows that TMA cannot address (odd K,
+# a row pitch that is not a multiple of 8 elements, a base off 16 bytes)
+# with A in 16-byte-pitched rows.  (id, M, N, K, W row pitch in elements
+# (None: K), W base offset in elements).
+LDG_CASES = [
+    ("k4090", 32, 4096, 4090, None, 0),
+    ("m1-k4090", 1, 4096, 4090, None, 0),
+    ("w-pitch", 32, 4096, 4096, 4098, 0),
+    ("w-offset", 8, 4096, 4096, None, 1),
+    ("m129-k4090", 129, 1031, 4090, None, 0),
+    ("m256-ragged", 256, 777, 1001, None, 0),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("case", LDG_CASES, ids=[c[0] for c in LDG_CASES])
+def test_sm_loaded_w_matches_aligned_copy(cuda_device, case, dtype):
+    """With no workspace, the tcgen05 kernel with W written into its stages
+    by the SM (path tc_ldg) gives the bits of the same plan on
+    16-byte-pitched copies."""
+    _, m, n, k, pitch, offset = case
+    a, w, bias = workloads.uniform_inputs(m, n, k, dtype=dtype)
+    pitch = k if pitch is None else pitch
+    store = torch.full((n * pitch + offset + 64,), float("nan"), dtype=dtype, device=cuda_device)
+    dw = store[offset:offset + n * pitch].view(n, pitch)[:, :k]
+    dw.copy_(w.to(cuda_device))
+    da, db = aligned_copy(a, cuda_device), bias.to(cuda_device)
+    code = native.dtype_code(dtype)
+    need = native.linear_workspace_bytes(code, da.data_ptr(), da.stride(), dw.data_ptr(), dw.t().stride(), m, n, k)
+    # a repack workspace would hold the W copy alone (A is addressable); this
+    # call gets none, so W is loaded by the SM
+    assert need == -(-n * (-(-k // 8) * 8) * 2 // 256) * 256
+    epi = native.EPILOGUE_BIAS_SILU
+    out = torch.empty((m, n), dtype=dtype, device=cuda_device)
+    out_al = torch.empty_like(out)
+    path, split = native.linear(da, dw.t(), out, db, epi)
+    assert path == "tc_ldg"
+    if m > 1:
+        path_al, split_al = native.linear(da, aligned_copy(w, cuda_device).t(), out_al, db, epi)
+        assert path_al not in ("unaligned", "repacked", "tc_ldg") and split == split_al
+    else:
+        # M = 1 on aligned rows is a GEMV: check that the call repeats its bits.
+        native.linear(da, dw.t(), out_al, db, epi)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), out_al.view(torch.int16))
+    atol, rtol = (U_ATOL, U_RTOL) if dtype == torch.float16 else (0.05, 0.01)
+    oracle.compare(host(out), oracle.linear_reference(a, w, bias, silu=True, samples=8), atol, rtol)
+    # the storage around W is untouched NaN: nothing was written there
+    assert torch.isnan(store[:offset]).all() and torch.isnan(store[offset + n * pitch:]).all()
 
 
 def test_repacked_fused_chain_in_a_graph(cuda_device):
