@@ -376,3 +376,64 @@ def test_gather_static_rejects_slots_outside_the_scratch():
     if not torch.cuda.is_available():
         assert call(0) == 7
         assert call(native.STATIC_GATHER_SLOTS - 1) == 7
+
+
+def ldg_stage_image(mem: bytes, base: int, pitch: int, n_rows: int, k: int, k0: int) -> bytes:
+    """Host restatement of one 128-row x 64-K W stage written by the tc_ldg
+    producer (warps 2..5): lane t of the 128 producer threads owns chunk
+    c = t % 8 of rows t / 8 + 16 j; lo = the aligned granule holding the
+    chunk's first byte (read if it starts before the row's end), hi = the
+    next lane's lo, or, for c = 7, its own load of the next granule; the
+    32-byte window is shifted by the row's byte offset, columns >= K and rows
+    >= N are zero, and chunk c of row r lands at r * 128 + (c ^ (r % 8)) * 16.
+    `mem` holds the bytes at addresses 0 .. len(mem)."""
+    stage = bytearray(128 * 128)
+    g16 = lambda addr: mem[addr:addr + 16] if addr + 16 <= len(mem) else bytes(16)
+    for t in range(128):
+        c = t % 8
+        for j in range(8):
+            r = t // 8 + 16 * j
+            out = bytes(16)
+            if r < n_rows and k - (k0 + 8 * c) > 0:
+                row_begin = base + r * pitch
+                row_end = row_begin + 2 * k
+                first = row_begin + 2 * k0
+                g = (first & ~15) + 16 * c
+                shift = first & 15
+                lo = g16(g) if g < row_end else bytes(16)
+                if c == 7:
+                    hi = g16(g + 16) if shift and g + 16 < row_end else bytes(16)
+                else:
+                    hi = g16(g + 16) if g + 16 < row_end else bytes(16)  # the next lane's lo
+                window = lo + hi
+                out = bytearray(window[shift:shift + 16])
+                valid = k - (k0 + 8 * c)
+                for e in range(8):
+                    if e >= valid:
+                        out[2 * e:2 * e + 2] = b"\0\0"
+                out = bytes(out)
+            off = r * 128 + ((c ^ (r % 8)) * 16)
+            stage[off:off + 16] = out
+    return bytes(stage)
+
+
+@pytest.mark.parametrize("k,pitch,base", [(4090, 4090, 64), (4096, 4098, 128), (4096, 4096, 130), (1001, 1001, 70),
+                                          (131, 135, 2)])
+def test_ldg_stage_restatement(k, pitch, base):
+    """The producer's granule / shuffle / shift mapping and its swizzle
+    placement give exactly the 128-byte-swizzled K-major tile of the rows
+    (what a TMA load with out-of-bounds zero fill would write)."""
+    rng = np.random.default_rng(k + pitch + base)
+    n_rows = 100  # ragged: rows >= N are zero
+    mem = rng.integers(0, 256, size=base + n_rows * pitch * 2 + 64, dtype=np.uint8).tobytes()
+    for k0 in range(0, k, 64 * max(1, k // 256)):
+        got = ldg_stage_image(mem, base, pitch * 2, n_rows, k, k0)
+        want = bytearray(128 * 128)
+        for r in range(min(n_rows, 128)):
+            row = mem[base + r * pitch * 2 + 2 * k0: base + r * pitch * 2 + 2 * min(k, k0 + 64)]
+            dense = row + bytes(128 - len(row))
+            for off in range(0, 128, 16):
+                linear = r * 128 + off
+                swz = linear ^ (((linear >> 7) & 7) << 4)  # 128-byte swizzle: bits 4-6 ^= bits 7-9
+                want[swz:swz + 16] = dense[off:off + 16]
+        assert got == bytes(want), f"k0={k0}"
