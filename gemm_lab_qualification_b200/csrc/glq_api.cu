@@ -101,8 +101,9 @@ struct StaticScratchState {
 
 StaticScratchState g_static_scratch[kMaxDevices];
 
-// Device address of g_static_gather_scratch on the current device, zeroed
-// once (first call per device, with that device current).
+// Device address of g_static_gather_scratch on the current device (looked
+// up once per device, with that device current).  Nothing is written here:
+// every call clears its own slot on its stream.
 int static_gather_scratch(unsigned int** out) {
   DeviceState* dev_state = nullptr;
   const int v = device_state(&dev_state);
@@ -115,9 +116,7 @@ int static_gather_scratch(unsigned int** out) {
   StaticScratchState& st = g_static_scratch[dev];
   std::call_once(st.once, [&st] {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_static_gather_scratch) != cudaSuccess ||
-        cudaMemset(ptr, 0, sizeof(g_static_gather_scratch)) != cudaSuccess ||
-        cudaDeviceSynchronize() != cudaSuccess) {
+    if (cudaGetSymbolAddress(&ptr, g_static_gather_scratch) != cudaSuccess) {
       cudaGetLastError();
       st.status = GLQ_ERR_CUDA;
       return;
@@ -292,6 +291,90 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   return GLQ_OK;
 }
 
+// A validated, planned fused-gather call (glq_linear_gather and its
+// allocation-free variant share it): nothing runs on the device until
+// launch_gather.
+struct GatherCall {
+  Problem p;
+  Gather g;
+  Choice c;
+  DeviceState* dev;
+};
+
+int prepare_gather(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride, const void* B,
+                   int64_t b_k_stride, int64_t b_n_stride, const void* bias, int epilogue, void* const* y_ranks,
+                   int64_t y_row_stride, int64_t y_col_offset, int64_t M, int64_t N, int64_t K, int split_k, int rank,
+                   int world, uint64_t* const* signal_ranks, uint64_t epoch, unsigned int flags, bool no_counter,
+                   GatherCall* call) {
+  int v = validate(dtype, epilogue, M, N, K, split_k);
+  if (v != GLQ_OK) return v;
+  if ((flags & ~(GLQ_FLAG_NO_PDL | GLQ_FLAG_STATIC_WEIGHTS)) != 0) return GLQ_ERR_INVALID_ARGUMENT;
+  if (world < 1 || world > GLQ_MAX_RANKS || rank < 0 || rank >= world) return GLQ_ERR_INVALID_ARGUMENT;
+  if (M <= 0 || N <= 0 || K <= 0) return GLQ_ERR_SHAPE;
+  if (A == nullptr || B == nullptr || y_ranks == nullptr || signal_ranks == nullptr || no_counter || epoch == 0) {
+    return GLQ_ERR_INVALID_ARGUMENT;
+  }
+  if (epilogue != GLQ_EPILOGUE_NONE && bias == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
+  if (y_col_offset < 0 || y_row_stride < y_col_offset + N) return GLQ_ERR_OUTPUT_LAYOUT;
+  // 16-bit elements: every element pointer is 2-byte aligned (the kernels'
+  // 16-bit loads and stores fault on an odd address).
+  auto odd = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 1u) != 0; };
+  if (odd(A) || odd(B) || (bias != nullptr && odd(bias))) return GLQ_ERR_INVALID_ARGUMENT;
+  constexpr int64_t esz = 2;
+  Gather& g = call->g;
+  g = Gather{};
+  g.rank = rank;
+  g.world = world;
+  for (int r = 0; r < world; ++r) {
+    if (y_ranks[r] == nullptr || signal_ranks[r] == nullptr || odd(y_ranks[r])) return GLQ_ERR_INVALID_ARGUMENT;
+    g.y[r] = static_cast<char*>(y_ranks[r]) + y_col_offset * esz;
+    g.signal[r] = reinterpret_cast<unsigned long long*>(signal_ranks[r]);
+  }
+  g.counter = nullptr;
+  g.epoch = static_cast<unsigned long long>(epoch);
+
+  Problem& p = call->p;
+  p = Problem{};
+  p.dtype = dtype;
+  p.a = A;
+  p.a_rs = a_row_stride;
+  p.a_cs = a_col_stride;
+  p.b = B;
+  p.b_ks = b_k_stride;
+  p.b_ns = b_n_stride;
+  p.bias = bias;
+  p.epilogue = epilogue;
+  p.y = g.y[rank];
+  p.ldy = y_row_stride;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  p.partial = nullptr;
+  p.flags = flags;
+  p.require_tc = 1;
+
+  v = device_state(&call->dev);
+  if (v != GLQ_OK) return v;
+  v = plan_problem(p, split_k, call->dev->sm_count, &call->c);
+  if (v != GLQ_OK) return v;
+  if (call->c.kernel != kKernelTc) return GLQ_ERR_INVALID_ARGUMENT;
+  return GLQ_OK;
+}
+
+int launch_gather(GatherCall* call, unsigned int* counter, cudaStream_t s, int* path_out, int* split_out) {
+  call->g.counter = counter;
+  const Choice& c = call->c;
+  const cudaError_t e =
+      launch_tc(call->p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, &call->g, call->dev->error_word, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return GLQ_ERR_CUDA;
+  }
+  if (path_out) *path_out = c.path;
+  if (split_out) *split_out = c.split;
+  return GLQ_OK;
+}
+
 }  // namespace glq
 
 using glq::Choice;
@@ -447,66 +530,14 @@ int glq_linear_gather(int dtype, const void* A, int64_t a_row_stride, int64_t a_
                       int64_t y_row_stride, int64_t y_col_offset, int64_t M, int64_t N, int64_t K, int split_k,
                       int rank, int world, uint64_t* const* signal_ranks, unsigned int* counter, uint64_t epoch,
                       void* stream, unsigned int flags, int* path_out, int* split_out) {
-  int v = glq::validate(dtype, epilogue, M, N, K, split_k);
-  if (v != GLQ_OK) return v;
-  if ((flags & ~(GLQ_FLAG_NO_PDL | GLQ_FLAG_STATIC_WEIGHTS)) != 0) return GLQ_ERR_INVALID_ARGUMENT;
-  if (world < 1 || world > GLQ_MAX_RANKS || rank < 0 || rank >= world) return GLQ_ERR_INVALID_ARGUMENT;
-  if (M <= 0 || N <= 0 || K <= 0) return GLQ_ERR_SHAPE;
-  if (A == nullptr || B == nullptr || y_ranks == nullptr || signal_ranks == nullptr || counter == nullptr ||
-      epoch == 0) {
-    return GLQ_ERR_INVALID_ARGUMENT;
-  }
-  if (epilogue != GLQ_EPILOGUE_NONE && bias == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
-  if (y_col_offset < 0 || y_row_stride < y_col_offset + N) return GLQ_ERR_OUTPUT_LAYOUT;
-  constexpr int64_t esz = 2;
-  glq::Gather g = {};
-  g.rank = rank;
-  g.world = world;
-  for (int r = 0; r < world; ++r) {
-    if (y_ranks[r] == nullptr || signal_ranks[r] == nullptr) return GLQ_ERR_INVALID_ARGUMENT;
-    g.y[r] = static_cast<char*>(y_ranks[r]) + y_col_offset * esz;
-    g.signal[r] = reinterpret_cast<unsigned long long*>(signal_ranks[r]);
-  }
-  g.counter = counter;
-  g.epoch = static_cast<unsigned long long>(epoch);
-
-  Problem p = {};
-  p.dtype = dtype;
-  p.a = A;
-  p.a_rs = a_row_stride;
-  p.a_cs = a_col_stride;
-  p.b = B;
-  p.b_ks = b_k_stride;
-  p.b_ns = b_n_stride;
-  p.bias = bias;
-  p.epilogue = epilogue;
-  p.y = g.y[rank];
-  p.ldy = y_row_stride;
-  p.m = M;
-  p.n = N;
-  p.k = K;
-  p.partial = nullptr;
-  p.flags = flags;
-  p.require_tc = 1;
-
   if (path_out) *path_out = GLQ_PATH_EMPTY;
   if (split_out) *split_out = 1;
-  glq::DeviceState* dev = nullptr;
-  v = glq::device_state(&dev);
+  glq::GatherCall call;
+  const int v = glq::prepare_gather(dtype, A, a_row_stride, a_col_stride, B, b_k_stride, b_n_stride, bias, epilogue,
+                                    y_ranks, y_row_stride, y_col_offset, M, N, K, split_k, rank, world,
+                                    signal_ranks, epoch, flags, counter == nullptr, &call);
   if (v != GLQ_OK) return v;
-  Choice c;
-  v = glq::plan_problem(p, split_k, dev->sm_count, &c);
-  if (v != GLQ_OK) return v;
-  if (c.kernel != glq::kKernelTc) return GLQ_ERR_INVALID_ARGUMENT;
-  const cudaError_t e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, &g, dev->error_word,
-                                       static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return GLQ_ERR_CUDA;
-  }
-  if (path_out) *path_out = c.path;
-  if (split_out) *split_out = c.split;
-  return GLQ_OK;
+  return glq::launch_gather(&call, counter, static_cast<cudaStream_t>(stream), path_out, split_out);
 }
 
 int glq_linear_gather_static(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_stride,
@@ -518,19 +549,25 @@ int glq_linear_gather_static(int dtype, const void* A, int64_t a_row_stride, int
   if (path_out) *path_out = GLQ_PATH_EMPTY;
   if (split_out) *split_out = 1;
   if (counter_slot < 0 || counter_slot >= GLQ_STATIC_GATHER_SLOTS) return GLQ_ERR_SCRATCH;
+  // Everything that can refuse the call runs before the slot is touched, so a
+  // rejected call leaves a slot that another stream may be using alone.
+  glq::GatherCall call;
+  int v = glq::prepare_gather(dtype, A, a_row_stride, a_col_stride, B, b_k_stride, b_n_stride, bias, epilogue,
+                              y_ranks, y_row_stride, y_col_offset, M, N, K, split_k, rank, world, signal_ranks,
+                              epoch, flags, false, &call);
+  if (v != GLQ_OK) return v;
   unsigned int* scratch = nullptr;
-  const int v = glq::static_gather_scratch(&scratch);
+  v = glq::static_gather_scratch(&scratch);
   if (v != GLQ_OK) return v;
   unsigned int* counter = scratch + counter_slot;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   // The kernel leaves the counter at zero, but a call whose wait expired may
   // not have: start every call from zero, in stream order.
-  if (cudaMemsetAsync(counter, 0, sizeof(unsigned int), static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+  if (cudaMemsetAsync(counter, 0, sizeof(unsigned int), s) != cudaSuccess) {
     cudaGetLastError();
     return GLQ_ERR_CUDA;
   }
-  return glq_linear_gather(dtype, A, a_row_stride, a_col_stride, B, b_k_stride, b_n_stride, bias, epilogue,
-                           y_ranks, y_row_stride, y_col_offset, M, N, K, split_k, rank, world, signal_ranks,
-                           counter, epoch, stream, flags, path_out, split_out);
+  return glq::launch_gather(&call, counter, s, path_out, split_out);
 }
 
 int glq_linear_f16(const void* A, int64_t lda, int64_t a_col_stride, const void* B,

@@ -305,12 +305,16 @@ int glq_linear_gather(int dtype,
  * those of glq_linear_gather (the caller still passes the inputs, the
  * outputs and the signal slots), and nothing is allocated.
  *
- * The slot is cleared on the caller's stream before each launch.  All calls
+ * Every argument is checked before the slot is touched: a refused call
+ * (odd element pointer, bad rank or epoch, ...) returns its status without
+ * writing the array.  An accepted call clears its slot on the caller's
+ * stream (one stream-ordered 4-byte memset) and then launches.  All calls
  * share the array: calls that use the same slot and overlap on the GPU
  * (different streams, or several layers in flight) race and corrupt each
  * other's completion; give such calls different slots.  The first call on a
- * device looks up the array's device address and zeroes it once; make that
- * first call before any stream capture.
+ * device looks up the array's device address with that device current (a
+ * host-side query: nothing is written and the device is not synchronised);
+ * make that first call before any stream capture.
  *
  * No counterpart in the reference (it has no multi-GPU path and no
  * allocation-free entry points).

@@ -327,7 +327,7 @@ def gather_status(**over):
     args = dict(dtype=0, a=16, lda=4096, acs=1, b=16, bks=1, bns=4096, bias=16, epi=2, ldy=8192, off=4096,
                 m=32, n=4096, k=4096, split=0, rank=1, world=2, counter=16, epoch=1, flags=0)
     args.update(over)
-    ys = (VP * 2)(16, 16) if over.get("ys", True) else None
+    ys = (VP * 2)(16, 17 if over.get("ys_odd") else 16) if over.get("ys", True) else None
     sigs = (VP * 2)(16, 16) if over.get("sigs", True) else None
     counter = ctypes.cast(VP(args["counter"]), ctypes.POINTER(ctypes.c_uint)) if args["counter"] else None
     return lib.glq_linear_gather(args["dtype"], args["a"], args["lda"], args["acs"], args["b"], args["bks"],
@@ -353,6 +353,11 @@ def test_gather_argument_validation():
     assert gather_status(split=9) == 3
     assert gather_status(ldy=8000) == 5      # y_col_offset + N > row pitch
     assert gather_status(off=-1) == 5
+    # 16-bit elements at odd addresses never reach a kernel
+    assert gather_status(bias=17) == 1
+    assert gather_status(a=17) == 1
+    assert gather_status(b=17) == 1
+    assert gather_status(ys_odd=True) == 1
     # valid arguments reach the device check: no sm_100a GPU here
     if not torch.cuda.is_available():
         assert gather_status() == 7
@@ -376,6 +381,23 @@ def test_gather_static_rejects_slots_outside_the_scratch():
     if not torch.cuda.is_available():
         assert call(0) == 7
         assert call(native.STATIC_GATHER_SLOTS - 1) == 7
+
+
+def test_gather_static_validates_before_touching_its_slot():
+    """A call the library refuses (odd bias, bad rank, epoch 0) returns its
+    status before the slot is cleared or the device is set up, so it cannot
+    disturb another stream's call on the same slot."""
+    lib = native.library()
+    VP = ctypes.c_void_p
+    ys = (VP * 1)(16)
+    sigs = (VP * 1)(16)
+
+    def call(bias=16, rank=0, epoch=1):
+        return lib.glq_linear_gather_static(0, 16, 4096, 1, 16, 1, 4096, bias, 2, ys, 4096, 0, 32, 4096, 4096, 0,
+                                            rank, 1, sigs, 0, epoch, None, 0, None, None)
+    assert call(bias=17) == 1
+    assert call(rank=1) == 1
+    assert call(epoch=0) == 1
 
 
 def ldg_stage_image(mem: bytes, base: int, pitch: int, n_rows: int, k: int, k0: int) -> bytes:
