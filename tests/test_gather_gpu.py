@@ -94,14 +94,14 @@ def test_gather_consecutive_epochs_single_rank(cuda_device):
     expected = oracle.linear_reference(a, w, bias, silu=True)
     for epoch in (1, 2, 3):
         out.fill_(0)
-        native.linear_gather(da, db_w, db, native.EPILOGUE_BIAS_SILU, [out.data_ptr()], 4096, 0, 0,
-                             [sig.data_ptr()], counter.data_ptr(), epoch)
+        path = native.linear_gather(da, db_w, db, native.EPILOGUE_BIAS_SILU, [out.data_ptr()], 4096, 0, 0,
+                                    [sig.data_ptr()], counter.data_ptr(), epoch)
         torch.cuda.synchronize()
         oracle.compare(host(out), expected, U_ATOL, U_RTOL)
         assert int(sig[0]) == epoch and int(counter[0]) == 0
-    # same bits as the plain call
+    # same bits as the plain call on the same (tiled, split-K) kernel
     plain = torch.empty_like(out)
-    native.linear(da, db_w, plain, db, native.EPILOGUE_BIAS_SILU)
+    assert native.linear(da, db_w, plain, db, native.EPILOGUE_BIAS_SILU, split_k=path[1]) == path
     torch.cuda.synchronize()
     assert torch.equal(plain.view(torch.int16), out.view(torch.int16))
 
