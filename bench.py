@@ -705,13 +705,19 @@ def multi_gpu(args, torch, dist, dev, world: int, rank: int) -> dict:
         host_us[label] = (time.perf_counter() - t0) * 1e6 / args.inner
         torch.cuda.synchronize()
     hold = max(400.0, 3.0 * args.inner * max(host_us.values()))
+    # Every sample starts with the ranks' streams lined up on the device (a
+    # one-element all-reduce), so the timed calls measure the layer in step,
+    # as consecutive layers of a model run, not the ranks' host launch skew.
+    token = torch.zeros(1, dtype=torch.float32, device=dev)
+    align = lambda: dist.all_reduce(token)
     raws = {}
     for label, fn in (("fused", fused_step), ("nccl", nccl_step)):
-        device_measure({label: fn}, rounds=args.warmup, inner=args.inner, hold_us=hold)
+        device_measure({label: fn}, rounds=args.warmup, inner=args.inner, hold_us=hold, align=align)
         dist.barrier()
         torch.cuda.synchronize()
         with ClockSampler(dev.index) as clocks:
-            raws[label] = device_measure({label: fn}, rounds=args.steps, inner=args.inner, hold_us=hold)[label]
+            raws[label] = device_measure({label: fn}, rounds=args.steps, inner=args.inner, hold_us=hold,
+                                         align=align)[label]
             torch.cuda.synchronize()
         if label == "fused":
             clock_summary = clocks.summary()
@@ -804,9 +810,11 @@ def sharded_shapes(args, torch, dist, dev, world: int, rank: int) -> list[dict]:
             host_us = (time.perf_counter() - t0) * 1e6 / inner
             torch.cuda.synchronize()
             hold = max(400.0, 3.0 * inner * host_us)
-            device_measure({"x": call}, rounds=2, inner=inner, hold_us=hold)
+            token = torch.zeros(1, dtype=torch.float32, device=dev)
+            align = lambda: dist.all_reduce(token)
+            device_measure({"x": call}, rounds=2, inner=inner, hold_us=hold, align=align)
             dist.barrier()
-            raw = device_measure({"x": call}, rounds=rounds, inner=inner, hold_us=hold)["x"]
+            raw = device_measure({"x": call}, rounds=rounds, inner=inner, hold_us=hold, align=align)["x"]
             dist.barrier()
             t = torch.tensor([statistics.median(raw)], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -875,7 +883,8 @@ def run_native(args) -> int:
                                "m": m, "n": n_total, "k": K_DIM, "n_per_rank": ns,
                                "parallelism": f"tp{world} (N-sharded, weak scaling)",
                                "timing": f"CUDA events around {args.inner} back-to-back layer calls behind a GPU "
-                                         "hold, p50 of span/inner, max over ranks",
+                                         "hold, the ranks' streams lined up by a one-element all-reduce before "
+                                         "each sample, p50 of span/inner, max over ranks",
                                "l2": f"inputs larger than L2: {res['copies']} rotating W-slice copies per rank"},
                     "impl": "native", "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
                     "local_path": list(res["path"]),

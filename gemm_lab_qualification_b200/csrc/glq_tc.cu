@@ -723,60 +723,61 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
     ptx::tmem_dealloc(tmem_d, Cfg::kTmemCols);
   }
 
-  // ---- Fused gather completion.  After the CTA barrier, thread 0 fences
-  // at GPU scope (cumulative over the CTA's stores, local and peer) and
-  // counts the CTA in with a fire-and-forget add: a release pattern that
-  // CTA 0's acquire pattern (relaxed poll, then fence) synchronises with on
-  // this GPU.  CTA 0 of the grid waits until every CTA has counted in,
-  // resets the counter, fences at system scope (so every CTA's stores
-  // precede, in causality order, what follows), writes the epoch into this
-  // rank's slot of every rank's signal array and waits, bounded, until every
-  // rank has written its slot here, one lane per rank reading the slots with
-  // system-scope acquire loads (which order the peers' slices before the
-  // kernel's end).
-  // Only CTA 0 pays a system-scope fence: hundreds of concurrent ones
-  // serialise.  The kernel therefore completes only when this rank's output
-  // holds all slices.  Every wait is bounded; on expiry the device error
-  // word gets kErrTimeoutPeer and the kernel returns.
+  // ---- Fused gather completion.  The output tile left as 16-byte stores
+  // (generic proxy) to this rank's Y and over NVLink to every peer's.  After
+  // the CTA barrier, thread 0 fences at GPU scope (cumulative over the CTA's
+  // stores, local and peer) and counts the CTA in with an acq_rel atomic
+  // add; the CTA whose add completes the count synchronises with every other
+  // CTA's release on this GPU, resets the counter, fences at system scope (so
+  // every CTA's stores precede, in causality order, what follows), writes the
+  // epoch into this rank's slot of every rank's signal array and waits,
+  // bounded, until every rank has written its slot here, one lane per rank
+  // reading the slots with system-scope acquire loads (which order the
+  // peers' slices before the kernel's end).  Only that one CTA pays a
+  // system-scope fence (hundreds of concurrent ones serialise), and no CTA
+  // waits for its NVLink writes to land before counting in.  The kernel
+  // completes only when this rank's output holds all slices.  Every wait is
+  // bounded; on expiry the device error word gets kErrTimeoutPeer and the
+  // kernel returns.
   if constexpr (GATHER) {
     __syncthreads();
+    bool last = false;
     if (threadIdx.x == 0) {
+      // This CTA's output stores (every thread's, local and over NVLink,
+      // ordered before by the barrier) are released at GPU scope with the
+      // count; the CTA whose increment completes the count is the last and
+      // publishes for the grid.
       ptx::fence_acq_rel_gpu();
-      ptx::red_add_relaxed_gpu(args.counter, 1u);
-    }
-    if (warp == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
       const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
-      const uint64_t t0 = ptx::globaltimer_ns();
-      uint32_t polls = 0;
-      auto expired = [&]() {
-        return (++polls & 63u) == 0u && (ptx::globaltimer_ns() - t0 > kWaitBudgetNs || polls > (1u << 26));
-      };
-      bool ok = true;
-      if (lane == 0) {
-        while (ptx::ld_relaxed_gpu_u32(args.counter) < total) {
-          if (expired()) {
-            ok = false;
-            break;
-          }
-        }
-        if (ok) {
+      last = ptx::atom_add_acq_rel_gpu(args.counter, 1u) == total - 1u;
+    }
+    if (warp == 0) {
+      last = __shfl_sync(0xffffffffu, last ? 1 : 0, 0) != 0;
+      if (last) {
+        if (lane == 0) {
           *args.counter = 0u;  // every CTA of this grid has counted in
+          // The one system-scope fence of the grid: cumulative over every
+          // CTA's stores synchronised above, so they are visible to any
+          // rank that sees the epoch written after it.
           ptx::fence_acq_rel_sys();
           for (int r = 0; r < args.n_out; ++r) ptx::st_relaxed_sys_u64(args.sig_out[r] + args.rank, args.epoch);
         }
-      }
-      // Lane r waits for rank r's epoch (all ranks' slots polled at once).
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (ok && lane < args.n_out) {
-        while (ptx::ld_acquire_sys_u64(args.sig_in + lane) < args.epoch) {
-          if (expired()) {
-            ok = false;
-            break;
+        __syncwarp();
+        // Lane r waits for rank r's epoch (all ranks' slots polled at once).
+        const uint64_t t0 = ptx::globaltimer_ns();
+        uint32_t polls = 0;
+        bool ok = true;
+        if (lane < args.n_out) {
+          while (ptx::ld_acquire_sys_u64(args.sig_in + lane) < args.epoch) {
+            if ((++polls & 63u) == 0u && (ptx::globaltimer_ns() - t0 > kWaitBudgetNs || polls > (1u << 26))) {
+              ok = false;
+              break;
+            }
           }
         }
+        const bool all_ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0 && !all_ok) atomicOr(args.err, kErrTimeoutPeer);
       }
-      const bool all_ok = __all_sync(0xffffffffu, ok);
-      if (lane == 0 && !all_ok) atomicOr(args.err, kErrTimeoutPeer);
     }
   }
 }
@@ -935,7 +936,10 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
     if (bases_ok && ys_off + rows * TN * static_cast<uint32_t>(esz) <= Cfg::kPipeBytes) args.ys_offset = ys_off;
   }
   // Bulk copies need 16-byte row segments: every tile's valid width a multiple of 8.
-  args.bulk_out = (args.ys_offset != ~0u && p.n % 8 == 0) ? 1 : 0;
+  // Outputs leave by 16-byte stores from all threads (generic proxy): the
+  // grid's single system-scope fence then covers them, where bulk copies
+  // (async proxy) had to be awaited by every CTA before it could count in.
+  args.bulk_out = 0;
   const uint32_t body = dedicated ? Cfg::kPipeBytes + recv_bytes : Cfg::kPipeBytes;
   args.barrier_offset = (body + 15u) & ~15u;
   const uint32_t smem_bytes = 1024 + args.barrier_offset + Cfg::kBarrierBytes;

@@ -68,13 +68,18 @@ def hold_cycles(microseconds: float) -> int:
 
 
 def device_measure(functions: dict[str, Callable[[], object]], rounds: int, inner: int = 10, seed: int = 7,
-                   hold_us: float = 400.0) -> dict[str, list[float]]:
+                   hold_us: float = 400.0, align: Callable[[], object] | None = None) -> dict[str, list[float]]:
     """Per-call device milliseconds, ``rounds`` samples per function.
 
     Each sample: a GPU hold of ``hold_us`` (so the launches behind it queue
     up), a start event, ``inner`` back-to-back calls, an end event, all on the
     current stream; the sample is the span / ``inner``.  Functions are visited
     in a fresh shuffled order every round.  Returns the raw samples.
+
+    ``align`` (multi-GPU): enqueued before each sample's hold, it lines the
+    ranks' streams up on the device (e.g. a one-element collective), so that
+    every rank's hold ends at the same moment and a call that waits for its
+    peers does not absorb the ranks' host launch skew.
     """
     import torch
     stream = torch.cuda.current_stream()
@@ -86,6 +91,8 @@ def device_measure(functions: dict[str, Callable[[], object]], rounds: int, inne
         rng.shuffle(keys)
         for key in keys:
             start, end = events[key]
+            if align is not None:
+                align()
             torch.cuda._sleep(hold_cycles(hold_us))
             start.record(stream)
             fn = functions[key]
