@@ -148,15 +148,31 @@ OperandLayout classify(const Problem& p) {
   return L;
 }
 
-bool ldg_w(const Problem& p, const OperandLayout& L) {
-  return L.w_kmajor && !L.w_ok && L.a_ok && !p.require_tc && !small_problem(p.m, p.n, p.k);
+int raw_operands(const Problem& p, const OperandLayout& L) {
+  if (L.w_ok && L.a_ok) return 0;
+  if (!L.a_unit || !L.w_kmajor || p.require_tc || small_problem(p.m, p.n, p.k)) return -1;
+  RawClasses rc;
+  int raw = 0;
+  if (!L.w_ok) {
+    if (!raw_classes(p.b, p.n, p.k, p.b_ns, &rc)) return -1;
+    raw |= kRawW;
+  }
+  if (!L.a_ok) {
+    if (!raw_classes(p.a, p.m, p.k, p.a_rs, &rc)) return -1;
+    raw |= kRawA;
+  }
+  return raw;
 }
 
 bool repack_plan(const Problem& p, RepackPlan* r) {
   *r = RepackPlan();
-  // Small problems run the small kernel on the operands as they are.
+  // Small problems run the small kernel on the operands as they are, and
+  // the tcgen05 kernel aligns K-contiguous rows itself up to
+  // kRawCopyAboveTokens tokens.
   if (p.m <= 0 || p.n <= 0 || p.k <= 0 || small_problem(p.m, p.n, p.k)) return false;
   const OperandLayout L = classify(p);
+  const int raw = raw_operands(p, L);
+  if (raw == 0 || (raw > 0 && p.m <= kRawCopyAboveTokens)) return false;
   auto bytes = [](int64_t rows, int64_t cols) {
     return (static_cast<size_t>(rows) * static_cast<size_t>(repack_pitch(cols)) * 2u + 255u) / 256u * 256u;
   };
@@ -210,7 +226,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->tile_n = 128;
   c->stages = 0;
   c->w_mn = 0;
-  c->w_ldg = 0;
+  c->raw = 0;
   if (p.m == 0 || p.n == 0) {
     c->path = GLQ_PATH_EMPTY;
     c->kernel = kKernelNone;
@@ -227,22 +243,23 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
     c->kernel = small_problem(p.m, p.n, p.k) ? kKernelSmall : kKernelGeneric;
     return GLQ_OK;
   }
-  // K-major W rows that TMA cannot address (odd K, an odd row pitch or
-  // base), with an addressable A: the tcgen05 kernel loads W by the SM
-  // (4x the generic kernel; a call with a repack workspace copies W instead).
-  const bool ldg = ldg_w(p, L);
-  if ((!L.w_ok || !L.a_ok) && !ldg) {
+  // K-contiguous rows that TMA cannot address (odd K, a row pitch or base
+  // off 16 bytes) in either operand: the tcgen05 kernel loads them by row
+  // class and aligns them in shared memory (no copy, no workspace).
+  const int raw = raw_operands(p, L);
+  const bool staged = raw > 0;
+  if (raw < 0) {
     c->path = GLQ_PATH_UNALIGNED;
     c->kernel = small_problem(p.m, p.n, p.k) ? kKernelSmall : kKernelGeneric;
     return GLQ_OK;
   }
   c->w_mn = L.w_mnmajor ? 1 : 0;
-  c->w_ldg = ldg ? 1 : 0;
+  c->raw = staged ? raw : 0;
   // M = 1 runs a GEMV, except for a forced split of 4 or more: the register
   // GEMV then holds one or two rows per block and every block re-stages all
   // of A (19 us at S = 8 vs 9.9 us for the tcgen05 split, which writes the
   // same [S, 1, N] FP32 partials).
-  if (p.m == 1 && L.w_kmajor && !p.require_tc && split_k < 4 && !ldg) {
+  if (p.m == 1 && L.w_kmajor && !p.require_tc && split_k < 4 && !staged) {
     const int sms = sm_count > 0 ? sm_count : 148;
     // The ring GEMV holds a whole SM per CTA, so with static weights (where a
     // call's weight stream should start while its predecessor drains) the
@@ -255,7 +272,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   }
   c->kernel = kKernelTc;
   c->tile_t = tc_token_tile(p.m);
-  c->tile_n = ldg ? 128 : tc_tile_rows(p.m, p.n);  // the SM-loaded W fills 128-row tiles
+  c->tile_n = staged ? 128 : tc_tile_rows(p.m, p.n);  // raw-staged operands use 128-row tiles
   const int64_t k_blocks = tc_k_blocks(p.k);
   const int64_t tiles = ((p.n + c->tile_n - 1) / c->tile_n) * ((p.m + c->tile_t - 1) / c->tile_t);
   const int sms = sm_count > 0 ? sm_count : 148;
@@ -275,11 +292,11 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   // Prefill-sized problems (256-token tiles, no split) with at least one
   // wave of 256 x 256 output tiles: two M = 128 MMAs per K step share the
   // token tile, doubling the FLOPs per staged byte.
-  if (c->split == 1 && c->tile_t == 256 && !ldg &&
+  if (c->split == 1 && c->tile_t == 256 && !staged &&
       ((p.n + 255) / 256) * ((p.m + 255) / 256) >= static_cast<int64_t>(sms)) {
     c->tile_n = 256;
   }
-  if (ldg) {
+  if (staged) {
     c->path = GLQ_PATH_TC_LDG;
   } else if (p.n % 128 != 0 || p.k % 64 != 0) {
     c->path = GLQ_PATH_TAIL;
@@ -463,12 +480,14 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
   v = glq::plan_problem(p, split_k, dev->sm_count, &c);
   if (v != GLQ_OK) return v;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Strided or unaligned operands with a workspace that holds their aligned
-  // copies: repack, then plan the copies (tcgen05 / GEMV instead of the
-  // generic kernel, or of the SM-loaded W, which streams W at about half the
-  // copy-then-TMA rate: 51 vs 25 us at 32 x 4096 x 4090).
+  // Strided operands, unaligned ones the tcgen05 kernel cannot stage itself
+  // (such as the lab's B = [K, N] with rows off 16 bytes), and unaligned
+  // K-contiguous ones of problems above kRawCopyAboveTokens tokens, with a
+  // workspace that holds their aligned copies: repack, then plan the copies
+  // (tcgen05 / GEMV instead of the generic or raw-staged kernel).
   glq::RepackPlan rp;
-  const bool repack = (c.kernel == glq::kKernelGeneric || c.w_ldg) && workspace != nullptr &&
+  const bool copies = c.kernel == glq::kKernelGeneric || (c.raw != 0 && p.m > glq::kRawCopyAboveTokens);
+  const bool repack = copies && workspace != nullptr &&
                       glq::aligned16(workspace) && glq::repack_plan(p, &rp) && workspace_bytes >= rp.bytes();
   if (repack) {
     if (glq::launch_repacks(p, rp, workspace, dev->sm_count, s) != cudaSuccess) {
@@ -484,7 +503,7 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
     if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) return GLQ_ERR_WORKSPACE;
     p.partial = static_cast<float*>(workspace);
   }
-  p.w_ldg = c.w_ldg;
+  p.raw = c.raw;
   cudaError_t e = cudaSuccess;
   switch (c.kernel) {
     case glq::kKernelFill: e = glq::launch_fill(p, s); break;

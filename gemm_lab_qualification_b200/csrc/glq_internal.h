@@ -41,7 +41,7 @@ struct Problem {
   float* partial;  // optional [split, m, n] FP32 split partials
   unsigned int flags;  // glq_flags
   int require_tc;      // 1: the tcgen05 kernel or an error (fused gather)
-  int w_ldg;           // 1: K-major W rows not TMA-addressable, loaded by the SM (tc kernel)
+  int raw;             // kRawW | kRawA: operands the tcgen05 kernel stages raw and aligns itself
 };
 
 // Fused all-gather of a column-parallel layer (glq_linear_gather): output
@@ -54,6 +54,45 @@ struct Gather {
   unsigned int* counter;
   unsigned long long epoch;
 };
+
+// Operands of the tcgen05 kernel that TMA cannot address as they are
+// (K-contiguous rows with a base or row pitch off 16 bytes): the kernel
+// loads them by row class and aligns them in shared memory.
+constexpr int kRawW = 1;
+constexpr int kRawA = 2;
+// Row classes of a raw operand: rows r == c (mod C) share one tensor map.
+constexpr int kMaxClasses = 8;
+
+// Row pitch (elements) the row classes are computed from: a single row has
+// no pitch, any multiple of 8 past its end serves.
+inline int64_t raw_pitch(int64_t rows, int64_t k, int64_t pitch) {
+  return rows <= 1 ? (k + 15) / 8 * 8 : pitch;
+}
+
+// Class count C (power of two, at most kMaxClasses) and the per-class
+// element offsets s_c (4 bits each) of a raw operand: rows x k, K
+// contiguous, row pitch `pitch` elements, base 2-byte aligned.  C * pitch
+// must be a multiple of 8 elements (16 bytes: a TMA row pitch) and at least
+// k + 8 (a class's rows, each read as k + s_c <= k + 7 elements, do not
+// overlap); false when no C <= kMaxClasses satisfies both.
+struct RawClasses {
+  int classes = 1;
+  unsigned int shifts = 0;
+};
+inline bool raw_classes(const void* base, int64_t rows, int64_t k, int64_t pitch, RawClasses* out) {
+  const uintptr_t b = reinterpret_cast<uintptr_t>(base);
+  if ((b & 1u) != 0 || rows <= 0 || k <= 0) return false;
+  const int64_t pe = raw_pitch(rows, k, pitch);
+  if (pe < k) return false;
+  int c = pe % 8 == 0 ? 1 : pe % 4 == 0 ? 2 : pe % 2 == 0 ? 4 : 8;
+  while (c < kMaxClasses && c * pe < k + 8) c *= 2;
+  if (c * pe < k + 8) return false;
+  const int64_t b0 = static_cast<int64_t>((b & 15u) >> 1);
+  out->classes = c;
+  out->shifts = 0;
+  for (int i = 0; i < c; ++i) out->shifts |= static_cast<unsigned int>((b0 + i * pe) & 7) << (4 * i);
+  return true;
+}
 
 // How the operands sit in memory: unit-stride dimensions and whether the
 // TMA kernels can address them (16-byte aligned bases and row pitches, rows
@@ -72,9 +111,12 @@ struct RepackPlan {
   size_t a_bytes = 0, w_bytes = 0;
   size_t bytes() const { return a_bytes + w_bytes; }
 };
-// True when W is K-major with rows TMA cannot address and A is addressable:
-// the tcgen05 kernel then loads W by the SM (path tc_ldg).
-bool ldg_w(const Problem& p, const OperandLayout& L);
+// kRawW / kRawA bits when the tcgen05 kernel can run with the operands that
+// TMA cannot address staged raw and aligned in shared memory (K-contiguous
+// rows, W K-major, row classes as raw_classes), 0 when both operands are
+// addressable, -1 when the problem needs the small or generic kernel or
+// aligned copies.
+int raw_operands(const Problem& p, const OperandLayout& L);
 // False when every operand is already TMA-addressable (or nothing to do).
 bool repack_plan(const Problem& p, RepackPlan* r);
 // The same problem reading the copies in `workspace`.
@@ -90,7 +132,7 @@ struct Choice {
   int tile_n;   // W rows per CTA of the tcgen05 kernel (128 or 256)
   int stages;   // TMA ring depth of the tcgen05 kernel (5: two CTAs per SM)
   int w_mn;     // 1: W = B^T is N-contiguous (B = [K, N]); MN-major W tiles
-  int w_ldg;    // 1: K-major W rows TMA cannot address, loaded by the SM (path tc_ldg)
+  int raw;      // kRawW | kRawA: operands staged raw and aligned by the tcgen05 kernel (path tc_ldg)
 };
 
 enum Kernel : int {
@@ -125,6 +167,13 @@ constexpr int kMaxAutoSplit = 4;
 // co-resident at that size).
 constexpr int kPairSplit = 8;
 constexpr int kPairStages = 4;
+
+// Operands the tcgen05 kernel can stage raw and align itself are copied
+// instead when the caller gives a repack workspace and the problem has more
+// than this many tokens: every token tile re-aligns the same W tiles, where
+// one copy serves them all (509 x 4099 x 4103: 103 us aligned in shared
+// memory, 56 us copied).
+constexpr int64_t kRawCopyAboveTokens = 128;
 
 // Token tile of the tcgen05 kernel for m tokens.
 inline int tc_token_tile(int64_t m) {

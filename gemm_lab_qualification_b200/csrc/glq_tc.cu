@@ -109,27 +109,78 @@ constexpr uint32_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
 // Two CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per block.
 constexpr uint32_t kPairSmemBudget = 233472u / 2u - 1024u;
 
+// Operands TMA cannot address directly (RAW kernels, bits kRawW / kRawA).
+// A raw row box: the stage's 64 K elements plus up to 7 elements of
+// in-granule offset, i.e. nine 16-byte granules.
+constexpr int kRawSpan = kTileK + 8;
+constexpr uint32_t kRawRowBytes = kRawSpan * 2;  // 144
+// TMA writes shared memory at 128-byte aligned addresses: the box of row
+// class c (rows_per_class raw rows) starts at c slots of
+// rows_per_class * 144 bytes rounded up to 128.
+__host__ __device__ constexpr uint32_t raw_class_offset(int c, int rows_per_class) {
+  return static_cast<uint32_t>(c) * ((static_cast<uint32_t>(rows_per_class) * kRawRowBytes + 127u) & ~127u);
+}
+// Raw bytes of `rows` tile rows in C classes, padding included, for the
+// worst class count (only classes of fewer than 8 rows need padding).
+__host__ __device__ constexpr uint32_t raw_area_bytes(int rows) {
+  uint32_t most = 0;
+  for (int c = 1; c <= 8; c *= 2) {
+    const uint32_t b = raw_class_offset(c, rows / c);
+    most = b > most ? b : most;
+  }
+  return most;
+}
+// Warps 2..5 turn raw stages into swizzled ones (idle during the main loop
+// otherwise): one per SM sub-partition, which is what bounds the shift.
+constexpr int kShiftWarps = 4;
+
 // BT: token tile (MMA N).  TN: W rows per CTA, one M = 128 MMA (and one TMEM
 // accumulator of BT columns) per 128 rows.  A 256-row tile moves W in 32 KB
 // TMA boxes, which streams HBM measurably better than 16 KB boxes at equal
 // bytes in flight.  STAGES: depth of the TMA ring; 4 stages of a small token
 // tile plus the split-K receive buffer keep a CTA under 113 KB of shared
 // memory, so two CTAs share an SM.
-template <int BT, int TN, int STAGES>
+//
+// Shared memory: STAGES load stages (what TMA writes: for each operand its
+// 128-byte-swizzled tile, or for a RAW operand its raw row boxes of 144
+// bytes per row), then, in RAW kernels, two aligned stages holding the
+// swizzled tiles of the RAW operands.
+template <int BT, int TN, int STAGES, int RAW = 0>
 struct TcConfig {
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128 is 16..256 step 16");
   static_assert(TN == 128 || TN == 256, "tile rows are one or two M=128 MMAs");
+  static_assert(RAW == 0 || TN == 128, "raw-staged kernels use 128-row W tiles");
+  static constexpr bool kRawW_ = (RAW & kRawW) != 0;
+  static constexpr bool kRawA_ = (RAW & kRawA) != 0;
   static constexpr int kAcc = TN / 128;
   static constexpr uint32_t kWTileBytes = TN * kTileK * 2;
   static constexpr uint32_t kATileBytes = BT * kTileK * 2;
-  static constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
+  // Load stage: the W part first, then A (1024-byte aligned when swizzled).
+  static constexpr uint32_t kLoadWBytes = kRawW_ ? raw_area_bytes(TN) : kWTileBytes;
+  static constexpr uint32_t kLoadABytes = kRawA_ ? raw_area_bytes(BT) : kATileBytes;
+  // Bytes TMA lands per stage (every box counts in full, zero fill included).
+  static constexpr uint32_t kLoadTx =
+      (kRawW_ ? TN * kRawRowBytes : kWTileBytes) + (kRawA_ ? BT * kRawRowBytes : kATileBytes);
+  // Load stages holding a swizzled tile start 1024-byte aligned; raw-only
+  // stages need the TMA's 128 bytes.
+  static constexpr uint32_t kStageAlign = (kRawW_ && kRawA_) ? 128u : 1024u;
+  static constexpr uint32_t kStageBytes = (kLoadWBytes + kLoadABytes + kStageAlign - 1u) / kStageAlign * kStageAlign;
   static constexpr int kStages = STAGES;
+  // Aligned stages of the RAW kernels (swizzled W if raw, then swizzled A if
+  // raw): two, so that the shift of stage i + 1 overlaps the MMA of stage i.
+  static constexpr int kShift = RAW == 0 ? 0 : 2;
+  static constexpr uint32_t kShiftAOffset = kRawW_ ? kWTileBytes : 0u;
+  static constexpr uint32_t kShiftBytes = (kRawW_ ? kWTileBytes : 0u) + (kRawA_ ? kATileBytes : 0u);
+  static constexpr uint32_t kShiftBase = (kStages * kStageBytes + 1023u) / 1024u * 1024u;
   static constexpr uint32_t kAccCols = kAcc * BT;
   static constexpr uint32_t kTmemCols =
       kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
-  static constexpr uint32_t kPipeBytes = kStages * kStageBytes;
-  static constexpr uint32_t kBarrierBytes = (2 * kStages + 2) * 8 + 16;
-  static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-B aligned");
+  static constexpr uint32_t kPipeBytes = kShiftBase + kShift * kShiftBytes;
+  // full/empty per load stage, full/empty per aligned stage, done, receive.
+  static constexpr int kBars = 2 * kStages + 2 * kShift + 2;
+  static constexpr uint32_t kBarrierBytes = kBars * 8 + 16;
+  static_assert(kLoadWBytes % 1024 == 0, "the A part of a load stage must stay 1024-B aligned");
+  static_assert(kShiftBytes % 1024 == 0, "aligned stages must stay 1024-B aligned");
   static_assert(1024 + kPipeBytes + kBarrierBytes <= kSmemLimit, "pipeline exceeds shared memory");
 };
 
@@ -157,137 +208,212 @@ struct TcArgs {
   int recv_overlaps;        // 1: the receive buffer reuses the drained pipeline stages
   uint32_t barrier_offset;  // mbarriers, bytes from the aligned base
   unsigned int flags;       // glq_flags
-  // LDG kernels: W [N, K] K-contiguous rows that TMA cannot address (row
-  // pitch or base not 16-byte aligned), loaded by the SM.
-  const void* w_ptr;
-  long long w_pitch_bytes;
+  // RAW kernels: rows of a raw operand are split into C classes (row
+  // r in class r % C, C a power of two); class c's rows start s_c elements
+  // into a 16-byte granule, 4 bits per class in *_shifts.
+  int w_classes, a_classes;
+  unsigned int w_shifts, a_shifts;
 };
 
-// W rows loaded by the SM instead of TMA: warps 2..5 fill each stage.
-constexpr int kLdgWarps = 4;
-constexpr int kLdgThreads = kLdgWarps * 32;
+// Tensor maps of a launch.  Plain kernels use w[0] and a[0]; a RAW operand
+// has one map per row class (unused classes repeat class 0).
+template <int RAW>
+struct alignas(64) TmaSet {
+  CUtensorMap w[(RAW & kRawW) ? kMaxClasses : 1];
+  CUtensorMap a[(RAW & kRawA) ? kMaxClasses : 1];
+};
 
-// ---- W producer for rows that TMA cannot address (LDG kernels).
+// ---- Raw-staged operands (RAW kernels).
 //
-// Thread t (0..127, warps 2..5) owns 16-byte chunk c = t % 8 of rows
-// r = t / 8 + 16 j (j = 0..7) of each 128-row x 64-K stage, so a warp covers
-// four rows of 128 contiguous bytes per step.  Chunk c of a row starts at
-// byte offset `shift` (the same for every chunk of the row) inside the
-// aligned granule G + 16 c; its bytes are that granule and the next one,
-// which is the neighbouring lane's granule (shuffle) except for c = 7, which
-// loads it.  A granule is read only if it holds bytes of the row (the first
-// always does unless the row is past N; the others are skipped past the
-// row's end), and an aligned 16-byte granule never crosses a page.  Columns
-// k >= K and rows n >= N are written as zero, as TMA's out-of-bounds fill
-// would.  Each chunk goes to its 128-byte-swizzle position (chunk c of row r
-// at r * 128 + ((c ^ (r % 8)) * 16)), the layout the K-major UMMA descriptor
-// reads; the writes are made visible to the tensor core with
-// fence.proxy.async before every thread's arrival on the stage's full
-// barrier.  All loads of a half stage are issued before any is used.
-template <typename T, int BT, int TN, int STAGES, typename FullBar, typename EmptyBar, typename Raise>
-__device__ __forceinline__ void ldg_fill_w(const TcArgs& args, uint8_t* smem, int kb_begin, int nkb, int tile_n,
-                                           FullBar full_bar, EmptyBar empty_bar, const volatile int* abort_flag,
-                                           Raise raise) {
-  using Cfg = TcConfig<BT, TN, STAGES>;
-  constexpr int kStages = Cfg::kStages;
-  constexpr int kRowsPerPass = kLdgThreads / 8;  // 16
-  constexpr int kPasses = TN / kRowsPerPass;      // 8
-  constexpr int kBatch = 4;                       // passes whose loads are in flight together
-  const int t = static_cast<int>(threadIdx.x) - 64;
-  const int lane = t & 31;
-  const int c = t & 7;
-  const uintptr_t wbase = reinterpret_cast<uintptr_t>(args.w_ptr);
-  const long long row_bytes = static_cast<long long>(args.k) * 2;
-  for (int i = 0; i < nkb; ++i) {
-    const int stage = i % kStages;
-    if (i >= kStages) {
-      bool ok = true;
-      if (lane == 0) {
-        ok = ptx::mbar_wait_bounded(empty_bar(stage), static_cast<uint32_t>(i / kStages - 1) & 1u, abort_flag,
-                                    kWaitBudgetNs);
-      }
-      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
-        if (lane == 0) raise(kErrTimeoutProducer);
-        return;
-      }
-    }
-    const long long k0 = static_cast<long long>(kb_begin + i) * kTileK;
-    uint8_t* const w_stage = smem + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
-#pragma unroll
-    for (int b = 0; b < kPasses; b += kBatch) {
-      uint4 lo[kBatch], hi[kBatch];
-      unsigned shift[kBatch];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int r = t / 8 + kRowsPerPass * (b + j);
-        const long long n = static_cast<long long>(tile_n) * TN + r;
-        lo[j] = make_uint4(0u, 0u, 0u, 0u);
-        hi[j] = make_uint4(0u, 0u, 0u, 0u);
-        shift[j] = 0;
-        if (n < args.n) {
-          const uintptr_t row_begin = wbase + static_cast<uintptr_t>(n * args.w_pitch_bytes);
-          const uintptr_t row_end = row_begin + static_cast<uintptr_t>(row_bytes);
-          const uintptr_t first = row_begin + static_cast<uintptr_t>(k0 * 2);
-          const uintptr_t g = (first & ~static_cast<uintptr_t>(15)) + 16u * static_cast<uintptr_t>(c);
-          shift[j] = static_cast<unsigned>(first & 15u);
-          if (g < row_end) lo[j] = __ldg(reinterpret_cast<const uint4*>(g));
-          if (c == 7 && shift[j] != 0 && g + 16 < row_end) hi[j] = __ldg(reinterpret_cast<const uint4*>(g + 16));
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const uint32_t nx = __shfl_down_sync(0xffffffffu, lo[j].x, 1);
-        const uint32_t ny = __shfl_down_sync(0xffffffffu, lo[j].y, 1);
-        const uint32_t nz = __shfl_down_sync(0xffffffffu, lo[j].z, 1);
-        const uint32_t nw = __shfl_down_sync(0xffffffffu, lo[j].w, 1);
-        if (c != 7) hi[j] = make_uint4(nx, ny, nz, nw);
-        const int r = t / 8 + kRowsPerPass * (b + j);
-        const long long n = static_cast<long long>(tile_n) * TN + r;
-        const long long valid = static_cast<long long>(args.k) - (k0 + 8 * c);
-        uint32_t out[4] = {0u, 0u, 0u, 0u};
-        if (n < args.n && valid > 0) {
-          const uint32_t w[8] = {lo[j].x, lo[j].y, lo[j].z, lo[j].w, hi[j].x, hi[j].y, hi[j].z, hi[j].w};
-          const unsigned q = shift[j] >> 2;
-          const unsigned bits = (shift[j] & 3u) * 8u;
-          uint32_t pick[5];
-#pragma unroll
-          for (int e = 0; e < 5; ++e) {
-            const uint32_t x0 = w[e], x1 = w[e + 1 < 8 ? e + 1 : 7], x2 = w[e + 2 < 8 ? e + 2 : 7],
-                           x3 = w[e + 3 < 8 ? e + 3 : 7];
-            pick[e] = q == 0 ? x0 : q == 1 ? x1 : q == 2 ? x2 : x3;
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) out[e] = __funnelshift_r(pick[e], pick[e + 1], bits);
-          if (valid < 8) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (2 * e >= valid) {
-                out[e] = 0u;
-              } else if (2 * e + 1 >= valid) {
-                out[e] &= 0xFFFFu;
-              }
-            }
-          }
-        }
-        *reinterpret_cast<uint4*>(w_stage + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
-      }
-    }
-    ptx::fence_proxy_async_smem();
-    ptx::mbar_arrive(full_bar(stage));
+// A K-contiguous operand whose base or row pitch P (elements) is not 16-byte
+// aligned cannot be a TMA source as it is, but every class of rows
+// r == c (mod C) can: with C a power of two such that C * P is a multiple of
+// 8 elements, the rows of class c sit C * P elements apart (a 16-byte
+// multiple), and the class's first row starts E_c = b0 + c * P elements past
+// the 16-byte boundary below the operand's base (b0 = the base's offset in
+// elements).  The host encodes one 2-D map per class whose origin is that
+// boundary plus (E_c & ~7) elements; a row's element k then sits at
+// x = k + s_c with s_c = E_c & 7, and the map's inner extent is K + s_c, so
+// TMA zero-fills exactly the columns k >= K.  The rows of a tile (W: 128
+// rows n0.., A: BT rows t0.., both multiples of 8) split into the C classes
+// as contiguous runs of class rows, so a stage is C boxes of
+// (rows / C) x 72 elements: the 64 K elements of the stage plus room for
+// the shift, landed unswizzled, row i of class c at i * 144 bytes past the
+// start of class c's box (raw_class_offset: every box starts 128-byte
+// aligned).  (C * P >= K + 8 is required, so that a class's rows never
+// overlap.)
+//
+// The shift warps (2..5) then write each row's 64 elements, shifted by s_c,
+// into the 128-byte-swizzled K-major tile the MMA reads: 16-byte chunk g of
+// a row is taken from its raw granules g and g + 1.  The chunks equal what
+// a TMA load with zero fill writes from an aligned copy of the operand, so
+// the MMA sums the same values in the same order.
+
+// 16 bytes starting S elements into the 32-byte window lo:hi.
+template <int S>
+__device__ __forceinline__ uint4 shift_by(const uint4& lo, const uint4& hi) {
+  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  constexpr int q = S >> 1;  // whole 32-bit words
+  if constexpr ((S & 1) == 0) {
+    return make_uint4(w[q], w[q + 1], w[q + 2], w[q + 3]);
+  } else {  // plus one element
+    return make_uint4(__funnelshift_r(w[q], w[q + 1], 16), __funnelshift_r(w[q + 1], w[q + 2], 16),
+                      __funnelshift_r(w[q + 2], w[q + 3], 16), __funnelshift_r(w[q + 3], w[q + 4], 16));
   }
 }
 
-// LDG: the W tiles are written into the swizzled stages by warps 2..5 from
-// plain 16-byte loads (K-major W, 128-row tiles, no gather); two CTAs per SM
-// must still fit, so these instantiations are capped at 128 registers.
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, bool LDG = false>
-__global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
-    tc_linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                     const __grid_constant__ CUtensorMap tmap_a, const TcArgs args) {
-  static_assert(!LDG || (!WMN && !GATHER && TN == 128), "SM-loaded W: K-major 128-row tiles only");
-  using Cfg = TcConfig<BT, TN, STAGES>;
-  constexpr uint32_t kWTileBytes = Cfg::kWTileBytes;
+// The same for a per-lane shift, without branches: words s / 2 .. s / 2 + 4
+// of the window picked by two levels of selects, then each output word is
+// the byte permutation of two neighbours (a half-word shift for odd s).
+__device__ __forceinline__ uint4 shift_window(const uint4& lo, const uint4& hi, unsigned s) {
+  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  const bool q1 = (s & 2u) != 0, q2 = (s & 4u) != 0;
+  uint32_t p[5];
+#pragma unroll
+  for (int e = 0; e < 5; ++e) {
+    const uint32_t low = q1 ? w[e + 1] : w[e];
+    const uint32_t high = q1 ? w[e + 3] : w[e + 2];
+    p[e] = q2 ? high : low;  // w[e + s / 2]
+  }
+  const unsigned sel = (s & 1u) ? 0x5432u : 0x3210u;
+  return make_uint4(__byte_perm(p[0], p[1], sel), __byte_perm(p[1], p[2], sel), __byte_perm(p[2], p[3], sel),
+                    __byte_perm(p[3], p[4], sel));
+}
+
+// A batch of N chunks that share the shift S: shift and store.
+template <int S, int N>
+__device__ __forceinline__ void store_shifted(const uint4 (&lo)[N], const uint4 (&hi)[N], uint8_t* const (&out)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) *reinterpret_cast<uint4*>(out[j]) = shift_by<S>(lo[j], hi[j]);
+}
+
+// Rows [0, ROWS) of one raw load stage -> the swizzled K-major tile at dst.
+// Raw rows are taken in class order in warp steps of four rows (lane l:
+// row l / 8 of the four, chunk g = l % 8); shift warp w takes the
+// contiguous block of steps [w * ROWS / 16, (w + 1) * ROWS / 16), in
+// batches of up to four steps.  A batch of 16 rows inside one class (every
+// W batch) has a warp-uniform shift, applied by a compile-time shift chosen
+// once per batch; batches that span classes (A tiles of 16 or 32 tokens in
+// 4 or 8 classes) shift per lane.  Each lane loads its two raw granules
+// itself.  `release` runs once every raw granule of this operand is in
+// registers, before the last batch is shifted and stored, so the load stage
+// is freed early.
+template <int ROWS, typename Release>
+__device__ __forceinline__ void shift_rows(const uint8_t* raw, uint8_t* dst, int classes, unsigned shifts,
+                                           Release release) {
+  static_assert(ROWS % 16 == 0, "tile rows come in multiples of 16");
+  constexpr int kPerWarp = ROWS / 16;                  // warp steps per shift warp
+  constexpr int kBatch = kPerWarp < 4 ? kPerWarp : 4;  // steps whose loads are issued together
+  const int wq = (static_cast<int>(threadIdx.x) >> 5) - 2;  // shift warp 0..3
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;
+  const int log_c = classes == 1 ? 0 : classes == 2 ? 1 : classes == 4 ? 2 : 3;
+  constexpr int kLogRows = ROWS == 16 ? 4 : ROWS == 32 ? 5 : ROWS == 64 ? 6 : ROWS == 128 ? 7 : 8;
+  static_assert((1 << kLogRows) == ROWS, "tile rows are a power of two");
+  const int log_rpc = kLogRows - log_c;  // rows per class = ROWS / C
+  const bool uniform = (1 << log_rpc) >= 4 * kBatch;  // a batch's rows lie in one class
+#pragma unroll
+  for (int b = 0; b < kPerWarp; b += kBatch) {
+    uint4 lo[kBatch], hi[kBatch];
+    uint8_t* out[kBatch];
+    unsigned sh[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int idx = 4 * (wq * kPerWarp + b + j) + (lane >> 3);  // class-order row index
+      const int c = idx >> log_rpc;
+      const int i = idx - (c << log_rpc);
+      const int rho = (i << log_c) + c;  // tile row
+      sh[j] = (shifts >> (4 * c)) & 7u;
+      out[j] = dst + rho * 128 + ((g ^ (rho & 7)) << 4);
+      const uint8_t* row = raw + raw_class_offset(c, 1 << log_rpc) + i * kRawRowBytes + 16 * g;
+      lo[j] = *reinterpret_cast<const uint4*>(row);
+      hi[j] = *reinterpret_cast<const uint4*>(row + 16);
+    }
+    if (b + kBatch >= kPerWarp) release();
+    if (uniform) {
+      switch (sh[0]) {
+        case 0: store_shifted<0>(lo, hi, out); break;
+        case 1: store_shifted<1>(lo, hi, out); break;
+        case 2: store_shifted<2>(lo, hi, out); break;
+        case 3: store_shifted<3>(lo, hi, out); break;
+        case 4: store_shifted<4>(lo, hi, out); break;
+        case 5: store_shifted<5>(lo, hi, out); break;
+        case 6: store_shifted<6>(lo, hi, out); break;
+        default: store_shifted<7>(lo, hi, out); break;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) *reinterpret_cast<uint4*>(out[j]) = shift_window(lo[j], hi[j], sh[j]);
+    }
+  }
+}
+
+// The shift warps' loop: for every K block of this CTA, wait for its load
+// stage and a free aligned stage, write the RAW operands' swizzled tiles,
+// release the load stage (one arrival per warp: the raw bytes are read) and
+// publish the aligned stage (every thread's writes made visible to the
+// tensor core by its own proxy fence, then one arrival per warp).
+template <int BT, int TN, int STAGES, int RAW, typename FullBar, typename EmptyBar, typename SFullBar,
+          typename SEmptyBar, typename Raise>
+__device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, int nkb, FullBar full_bar,
+                                           EmptyBar empty_bar, SFullBar sfull_bar, SEmptyBar sempty_bar,
+                                           const volatile int* abort_flag, Raise raise) {
+  using Cfg = TcConfig<BT, TN, STAGES, RAW>;
+  const int lane = threadIdx.x & 31;
+  for (int i = 0; i < nkb; ++i) {
+    const int stage = i % Cfg::kStages;
+    const int sst = i % Cfg::kShift;
+    bool ok = true;
+    if (lane == 0) {
+      ok = ptx::mbar_wait_bounded(full_bar(stage), static_cast<uint32_t>(i / Cfg::kStages) & 1u, abort_flag,
+                                  kWaitBudgetNs);
+      if (ok && i >= Cfg::kShift) {
+        ok = ptx::mbar_wait_bounded(sempty_bar(sst), static_cast<uint32_t>(i / Cfg::kShift - 1) & 1u, abort_flag,
+                                    kWaitBudgetNs);
+      }
+    }
+    if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+      if (lane == 0) raise(kErrTimeoutProducer);
+      return;
+    }
+    const uint8_t* load = smem + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
+    uint8_t* aligned = smem + Cfg::kShiftBase + static_cast<uint32_t>(sst) * Cfg::kShiftBytes;
+    // The load stage is released (one arrival per warp) once the last raw
+    // operand's granules are in registers; A (smaller) goes first.
+    auto release = [&]() {
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(empty_bar(stage));
+    };
+    auto keep = []() {};
+    if constexpr (Cfg::kRawA_) {
+      if constexpr (Cfg::kRawW_) {
+        shift_rows<BT>(load + Cfg::kLoadWBytes, aligned + Cfg::kShiftAOffset, args.a_classes, args.a_shifts, keep);
+      } else {
+        shift_rows<BT>(load + Cfg::kLoadWBytes, aligned + Cfg::kShiftAOffset, args.a_classes, args.a_shifts,
+                       release);
+      }
+    }
+    if constexpr (Cfg::kRawW_) shift_rows<TN>(load, aligned, args.w_classes, args.w_shifts, release);
+    // Every writer orders its stores before the tensor core's reads, then
+    // one arrival per warp (128 arrivals on one barrier serialise).
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(sfull_bar(sst));
+  }
+}
+
+// RAW: operands TMA cannot address are staged raw and aligned by warps 2..5
+// (K-major W, 128-row tiles, no gather); two CTAs per SM must still fit, so
+// these instantiations are capped at 128 registers.
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
+__global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
+    tc_linear_kernel(const __grid_constant__ TmaSet<RAW> maps, const TcArgs args) {
+  static_assert(RAW == 0 || (!WMN && !GATHER && TN == 128), "raw-staged operands: K-major 128-row tiles only");
+  using Cfg = TcConfig<BT, TN, STAGES, RAW>;
   constexpr int kStages = Cfg::kStages;
+  constexpr int kShift = Cfg::kShift;
+  // The MMA reads a load stage directly unless both operands are raw.
+  constexpr bool kMmaReadsLoad = !(Cfg::kRawW_ && Cfg::kRawA_);
 
   extern __shared__ uint8_t smem_dyn[];
   const uint32_t raw_base = ptx::smem_addr(smem_dyn);
@@ -296,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
   const uint32_t sbase = raw_base + pad;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + args.barrier_offset);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_slot = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -314,8 +440,10 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
 
   auto full_bar = [&](int i) { return ptx::smem_addr(&bars[i]); };
   auto empty_bar = [&](int i) { return ptx::smem_addr(&bars[kStages + i]); };
-  const uint32_t done_bar = ptx::smem_addr(&bars[2 * kStages]);
-  const uint32_t recv_bar = ptx::smem_addr(&bars[2 * kStages + 1]);
+  auto sfull_bar = [&](int i) { return ptx::smem_addr(&bars[2 * kStages + i]); };
+  auto sempty_bar = [&](int i) { return ptx::smem_addr(&bars[2 * kStages + kShift + i]); };
+  const uint32_t done_bar = ptx::smem_addr(&bars[2 * kStages + 2 * kShift]);
+  const uint32_t recv_bar = ptx::smem_addr(&bars[2 * kStages + 2 * kShift + 1]);
 
   // Token columns of this tile and, for split-K, the 4-column groups this
   // CTA owns: groups are dealt to the S ranks as [r*G/S, (r+1)*G/S).
@@ -337,37 +465,54 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
   auto issue_w = [&](int i) {
     const int stage = i % kStages;
     const uint32_t w_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
-    ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
-    if constexpr (WMN) {
+    const int k0 = (kb_begin + i) * kTileK;
+    ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kLoadTx);
+    if constexpr (Cfg::kRawW_) {
+      // One box of TN / C rows x 72 elements per row class, unswizzled.
+      const int rows = TN / args.w_classes;
+      for (int c = 0; c < args.w_classes; ++c) {
+        ptx::tma_load_2d(w_dst + raw_class_offset(c, rows), &maps.w[c], k0,
+                         tile_n * rows, full_bar(stage), pol_w);
+      }
+    } else if constexpr (WMN) {
       // TN/64 boxes of 64 N-contiguous W rows x 64 K rows, 8 KB apart.
 #pragma unroll
       for (int j = 0; j < TN / 64; ++j) {
-        ptx::tma_load_2d(w_dst + static_cast<uint32_t>(j) * kMnBoxBytes, &tmap_w, tile_n * TN + 64 * j,
-                         (kb_begin + i) * kTileK, full_bar(stage), pol_w);
+        ptx::tma_load_2d(w_dst + static_cast<uint32_t>(j) * kMnBoxBytes, &maps.w[0], tile_n * TN + 64 * j, k0,
+                         full_bar(stage), pol_w);
       }
     } else {
-      ptx::tma_load_2d(w_dst, &tmap_w, (kb_begin + i) * kTileK, tile_n * TN, full_bar(stage), pol_w);
+      ptx::tma_load_2d(w_dst, &maps.w[0], k0, tile_n * TN, full_bar(stage), pol_w);
     }
   };
   auto issue_a = [&](int i) {
     const int stage = i % kStages;
-    const uint32_t a_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes + kWTileBytes;
-    ptx::tma_load_2d(a_dst, &tmap_a, (kb_begin + i) * kTileK, tile_t * BT, full_bar(stage), pol_a);
+    const uint32_t a_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes + Cfg::kLoadWBytes;
+    const int k0 = (kb_begin + i) * kTileK;
+    if constexpr (Cfg::kRawA_) {
+      const int rows = BT / args.a_classes;
+      for (int c = 0; c < args.a_classes; ++c) {
+        ptx::tma_load_2d(a_dst + raw_class_offset(c, rows), &maps.a[c], k0,
+                         tile_t * rows, full_bar(stage), pol_a);
+      }
+    } else {
+      ptx::tma_load_2d(a_dst, &maps.a[0], k0, tile_t * BT, full_bar(stage), pol_a);
+    }
   };
   auto issue = [&](int i) {
-    if constexpr (LDG) {
-      // The W half of the stage arrives through the producer warps' arrivals.
-      ptx::mbar_arrive_expect_tx(full_bar(i % kStages), Cfg::kATileBytes);
-    } else {
-      issue_w(i);
-    }
+    issue_w(i);
     issue_a(i);
   };
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
-      // LDG: thread 0 (A, expect_tx) plus every W producer thread arrives.
-      ptx::mbar_init(full_bar(i), LDG ? 1 + kLdgThreads : 1);
-      ptx::mbar_init(empty_bar(i), 1);
+      ptx::mbar_init(full_bar(i), 1);
+      // A load stage is free once the MMA has read it (tcgen05.commit) and,
+      // in RAW kernels, once every shift warp has read its raw rows.
+      ptx::mbar_init(empty_bar(i), (RAW != 0 ? kShiftWarps : 0) + (kMmaReadsLoad ? 1 : 0));
+    }
+    for (int i = 0; i < kShift; ++i) {
+      ptx::mbar_init(sfull_bar(i), kShiftWarps);
+      ptx::mbar_init(sempty_bar(i), 1);
     }
     ptx::mbar_init(done_bar, 1);
     ptx::mbar_init(recv_bar, 1);
@@ -379,8 +524,8 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
       ptx::mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(split - 1) * TN *
                                                static_cast<uint32_t>(own_width) * 16u);
     }
-    ptx::prefetch_tensormap(&tmap_w);
-    ptx::prefetch_tensormap(&tmap_a);
+    for (int c = 0; c < ((RAW & kRawW) ? args.w_classes : 1); ++c) ptx::prefetch_tensormap(&maps.w[c]);
+    for (int c = 0; c < ((RAW & kRawA) ? args.a_classes : 1); ++c) ptx::prefetch_tensormap(&maps.a[c]);
     pol_w = ptx::policy_evict_first();
     pol_a = ptx::policy_evict_last();
     // Start the stream before anything else: the first kStages stages are
@@ -389,17 +534,13 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
     // caller declared the weights static) is read only after the dependency
     // wait.
     const int first = nkb < kStages ? nkb : kStages;
-    const bool static_w = !LDG && (args.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
+    const bool static_w = RAW == 0 && (args.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
     if (static_w) {
       for (int i = 0; i < first; ++i) issue_w(i);
     }
     ptx::grid_dependency_wait();
     for (; issued < first; ++issued) {
-      if constexpr (LDG) {
-        ptx::mbar_arrive_expect_tx(full_bar(issued), Cfg::kATileBytes);
-      } else {
-        if (!static_w) issue_w(issued);
-      }
+      if (!static_w) issue_w(issued);
       issue_a(issued);
     }
     *issued_slot = issued;
@@ -439,11 +580,11 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
   // the wait during the main loop; when the buffer reuses the pipeline it is
   // armed only after the main loop.
   const bool recv_dedicated = split > 1 && !args.recv_overlaps;
-  // W producer warps (LDG) wait after their loop instead.
-  const bool ldg_producer = LDG && warp >= 2 && warp < 2 + kLdgWarps;
+  // The shift warps (RAW) wait after their loop instead.
+  const bool shifter = RAW != 0 && warp >= 2 && warp < 2 + kShiftWarps;
   if (recv_dedicated) {
     ptx::cluster_arrive_relaxed();
-    if (warp >= 2 && !ldg_producer) ptx::cluster_wait();
+    if (warp >= 2 && !shifter) ptx::cluster_wait();
   }
 
   if (warp == 0) {
@@ -471,14 +612,24 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
       for (int i = 0; i < nkb; ++i) {
         const int stage = i % kStages;
         const uint32_t round = static_cast<uint32_t>(i / kStages);
-        if (!ptx::mbar_wait_bounded(full_bar(stage), round & 1u, abort_flag, kWaitBudgetNs)) {
+        const int sst = kShift > 0 ? i % kShift : 0;
+        bool ok = true;
+        if (kMmaReadsLoad) ok = ptx::mbar_wait_bounded(full_bar(stage), round & 1u, abort_flag, kWaitBudgetNs);
+        if (kShift > 0 && ok) {
+          ok = ptx::mbar_wait_bounded(sfull_bar(sst), static_cast<uint32_t>(i / (kShift > 0 ? kShift : 1)) & 1u,
+                                      abort_flag, kWaitBudgetNs);
+        }
+        if (!ok) {
           raise(kErrTimeoutMma);
           break;
         }
         ptx::tc_fence_after_sync();
-        const uint32_t w_src = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
+        const uint32_t load = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
+        const uint32_t aligned = sbase + Cfg::kShiftBase + static_cast<uint32_t>(sst) * Cfg::kShiftBytes;
+        const uint32_t w_src = Cfg::kRawW_ ? aligned : load;
+        const uint32_t a_src = Cfg::kRawA_ ? aligned + Cfg::kShiftAOffset : load + Cfg::kLoadWBytes;
         const uint64_t w_desc = WMN ? ptx::umma_desc_mn_sw128(w_src) : ptx::umma_desc_k_sw128(w_src);
-        const uint64_t a_desc = ptx::umma_desc_k_sw128(w_src + kWTileBytes);
+        const uint64_t a_desc = ptx::umma_desc_k_sw128(a_src);
 #pragma unroll
         for (int kk = 0; kk < kTileK / 16; ++kk) {
           // Each MMA consumes K = 16.  The 128-row halves of a 256-row W
@@ -489,16 +640,19 @@ __global__ void __launch_bounds__(kThreads, LDG ? 2 : 1)
                             a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        ptx::tc_commit(empty_bar(stage));
+        if (kShift > 0) ptx::tc_commit(sempty_bar(sst));
+        if (kMmaReadsLoad) ptx::tc_commit(empty_bar(stage));
       }
       ptx::tc_commit(done_bar);
     }
-  } else if (ldg_producer) {
-    if constexpr (LDG) ldg_fill_w<T, BT, TN, STAGES>(args, smem, kb_begin, nkb, tile_n, full_bar, empty_bar,
-                                                      abort_flag, raise);
+  } else if (shifter) {
+    if constexpr (RAW != 0) {
+      shift_loop<BT, TN, STAGES, RAW>(args, smem, nkb, full_bar, empty_bar, sfull_bar, sempty_bar, abort_flag,
+                                      raise);
+    }
   }
   __syncwarp();
-  if (recv_dedicated && (warp < 2 || ldg_producer)) ptx::cluster_wait();
+  if (recv_dedicated && (warp < 2 || shifter)) ptx::cluster_wait();
 
   // ---- Epilogue: 8 warps (rows and chunks as assigned above).
   if (!ptx::mbar_wait_bounded(done_bar, 0u, abort_flag, kWaitBudgetNs)) {
@@ -816,18 +970,72 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, bool LDG = false>
+// One map per row class of a raw operand (rows x k, K contiguous, row pitch
+// `pitch` elements, 2-byte aligned base): class c's rows r = c, c + C, ...
+// as a 2-D tensor of (k + s_c) x rows_c elements, origin at the 16-byte
+// boundary at or below its first row's start, row pitch C * pitch; boxes of
+// (tile_rows / C) rows x kRawSpan, unswizzled, zero fill out of bounds.  A
+// class without rows repeats class 0's map: what it loads lands on tile rows
+// past the operand's end, whose results are never stored.
+bool encode_raw(CUtensorMap* maps, CUtensorMapDataType type, const void* base, int64_t rows, int64_t k,
+                int64_t pitch, int tile_rows, RawClasses* rc) {
+  if (!raw_classes(base, rows, k, pitch, rc)) return false;
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encoder();
+  if (encode == nullptr) return false;
+  const uintptr_t b = reinterpret_cast<uintptr_t>(base);
+  const uintptr_t b_aligned = b & ~static_cast<uintptr_t>(15);
+  const int64_t b0 = static_cast<int64_t>((b & 15u) >> 1);
+  const int64_t pe = raw_pitch(rows, k, pitch);
+  const int c_count = rc->classes;
+  for (int c = 0; c < kMaxClasses; ++c) {
+    const int64_t rows_c = c < c_count ? (rows - c + c_count - 1) / c_count : 0;
+    if (rows_c <= 0) {
+      maps[c] = maps[0];
+      continue;
+    }
+    const int64_t e = b0 + c * pe;
+    const int64_t s = e & 7;
+    void* origin = reinterpret_cast<void*>(b_aligned + static_cast<uintptr_t>((e - s) * 2));
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k + s), static_cast<cuuint64_t>(rows_c)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(c_count * pe * 2)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawSpan), static_cast<cuuint32_t>(tile_rows / c_count)};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&maps[c], type, 2, origin, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      return false;
+    }
+  }
+  return true;
+}
+
+// Load-ring depth of the RAW kernels at two CTAs per SM: W raw stages are
+// 2 KB larger than swizzled ones, so three fit beside the aligned stages;
+// with only A raw the W stream keeps the plain kernel's four.
+constexpr int raw_pair_stages(int raw) { return raw == kRawA ? kPairStages : 3; }
+
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
 cudaError_t set_attr() {
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, LDG>,
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, RAW>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
+}
+
+template <typename T, int RAW>
+cudaError_t set_attrs_raw() {
+  cudaError_t e;
+  constexpr int kPair = raw_pair_stages(RAW);
+  if ((e = set_attr<T, 16, 128, kPair, false, false, RAW>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 32, 128, kPair, false, false, RAW>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 16, 128, 8, false, false, RAW>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 32, 128, 8, false, false, RAW>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 64, 128, 6, false, false, RAW>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 128, 128, 4, false, false, RAW>()) != cudaSuccess) return e;
+  return set_attr<T, 256, 128, 2, false, false, RAW>();
 }
 
 template <typename T, int BT, int TN, int STAGES>
 cudaError_t set_attrs() {
   cudaError_t e;
-  if constexpr (TN == 128) {
-    if ((e = set_attr<T, BT, TN, STAGES, false, false, true>()) != cudaSuccess) return e;
-  }
   if ((e = set_attr<T, BT, TN, STAGES, false, false>()) != cudaSuccess) return e;
   if ((e = set_attr<T, BT, TN, STAGES, true, false>()) != cudaSuccess) return e;
   if ((e = set_attr<T, BT, TN, STAGES, false, true>()) != cudaSuccess) return e;
@@ -846,31 +1054,45 @@ cudaError_t set_attrs_all() {
   if ((e = set_attrs<T, 32, 128, 8>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 64, 128, 8>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 128, 128, 6>()) != cudaSuccess) return e;
-  return set_attrs<T, 256, 128, 4>();
+  if ((e = set_attrs<T, 256, 128, 4>()) != cudaSuccess) return e;
+  if ((e = set_attrs_raw<T, kRawW>()) != cudaSuccess) return e;
+  if ((e = set_attrs_raw<T, kRawA>()) != cudaSuccess) return e;
+  return set_attrs_raw<T, kRawW | kRawA>();
 }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, bool LDG = false>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
 cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
-  CUtensorMap tmap_w, tmap_a;
-  const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
+  TmaSet<RAW> maps;
+  RawClasses w_rc, a_rc;
   bool ok = true;
-  if constexpr (LDG) {
-    // W is read by the SM: no W tensor map (the kernel gets A's as a stand-in).
+  if constexpr ((RAW & kRawW) != 0) {
+    // W rows TMA cannot address as they are: one unswizzled map per row class.
+    ok = encode_raw(maps.w, Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ns, TN, &w_rc);
   } else if constexpr (WMN) {
     // B = [K, N]: rows k (pitch b_ks), N contiguous; boxes 64(n) x 64(k).
-    ok = encode_2d(&tmap_w, Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
+    ok = encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
   } else {
     // W = B^T: rows n (pitch b_ns), K contiguous; boxes 64(k) x TN.
     const int64_t w_pitch = p.n > 1 ? p.b_ns * esz : ((p.k * esz + 15) / 16) * 16;
-    ok = encode_2d(&tmap_w, Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, kTileK, TN);
+    ok = encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, kTileK, TN);
   }
-  // A: rows m (pitch a_rs), K contiguous; boxes 64(k) x BT.
-  if (!ok || !encode_2d(&tmap_a, Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, kTileK, BT)) {
-    return cudaErrorInvalidValue;
+  if constexpr ((RAW & kRawA) != 0) {
+    ok = ok && encode_raw(maps.a, Elem<T>::kTmaType, p.a, p.m, p.k, p.a_rs, BT, &a_rc);
+  } else {
+    // A: rows m (pitch a_rs), K contiguous; boxes 64(k) x BT.
+    const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
+    ok = ok && encode_2d(&maps.a[0], Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, kTileK, BT);
   }
-  if constexpr (LDG) tmap_w = tmap_a;
-  using Cfg = TcConfig<BT, TN, STAGES>;
+  if (!ok) return cudaErrorInvalidValue;
+  using Cfg = TcConfig<BT, TN, STAGES, RAW>;
+  // The raw boxes of the operands' row classes must fit their load-stage areas.
+  if constexpr ((RAW & kRawW) != 0) {
+    if (raw_class_offset(w_rc.classes, TN / w_rc.classes) > Cfg::kLoadWBytes) return cudaErrorInvalidValue;
+  }
+  if constexpr ((RAW & kRawA) != 0) {
+    if (raw_class_offset(a_rc.classes, BT / a_rc.classes) > Cfg::kLoadABytes) return cudaErrorInvalidValue;
+  }
   TcArgs args;
   args.m = static_cast<int>(p.m);
   args.n = static_cast<int>(p.n);
@@ -901,8 +1123,10 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   args.partial = p.partial;
   args.err = err;
   args.flags = p.flags;
-  args.w_ptr = LDG ? p.b : nullptr;
-  args.w_pitch_bytes = LDG && p.n > 1 ? p.b_ns * esz : 0;
+  args.w_classes = w_rc.classes;
+  args.w_shifts = w_rc.shifts;
+  args.a_classes = a_rc.classes;
+  args.a_shifts = a_rc.shifts;
   // Shared memory: [pipeline stages][split-K receive buffer][mbarriers].
   // The receive buffer ((split - 1) remote sources x TN rows x owned groups
   // x 16 B) gets its own
@@ -917,7 +1141,7 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
     stage_bytes = TN * groups * 16u;
   }
   // The two-CTAs-per-SM configuration keeps under half an SM.
-  constexpr bool kPair = TN == 128 && BT <= 32 && STAGES == kPairStages;
+  constexpr bool kPair = TN == 128 && BT <= 32 && STAGES == (RAW != 0 ? raw_pair_stages(RAW) : kPairStages);
   const uint32_t budget = kPair ? kPairSmemBudget : kSmemLimit;
   const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= budget;
   args.recv_offset = dedicated ? Cfg::kPipeBytes : 0;
@@ -960,27 +1184,39 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, LDG>, tmap_w, tmap_a, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, RAW>, maps, args);
 }
 
-// K-major W rows that TMA cannot address: the LDG kernels (128-row tiles).
-template <typename T>
-cudaError_t launch_ldg(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
+// Operands TMA cannot address as they are: the RAW kernels (128-row tiles).
+template <typename T, int RAW>
+cudaError_t launch_raw(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
                        cudaStream_t s) {
   if (tile_n != 128) return cudaErrorInvalidValue;
   if (stages == kPairStages) {
+    constexpr int kPair = raw_pair_stages(RAW);
     switch (tile_t) {
-      case 16: return launch_typed<T, 16, 128, kPairStages, false, false, true>(p, split, nullptr, err, s);
-      case 32: return launch_typed<T, 32, 128, kPairStages, false, false, true>(p, split, nullptr, err, s);
+      case 16: return launch_typed<T, 16, 128, kPair, false, false, RAW>(p, split, nullptr, err, s);
+      case 32: return launch_typed<T, 32, 128, kPair, false, false, RAW>(p, split, nullptr, err, s);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (tile_t) {
-    case 16: return launch_typed<T, 16, 128, 8, false, false, true>(p, split, nullptr, err, s);
-    case 32: return launch_typed<T, 32, 128, 8, false, false, true>(p, split, nullptr, err, s);
-    case 64: return launch_typed<T, 64, 128, 8, false, false, true>(p, split, nullptr, err, s);
-    case 128: return launch_typed<T, 128, 128, 6, false, false, true>(p, split, nullptr, err, s);
-    case 256: return launch_typed<T, 256, 128, 4, false, false, true>(p, split, nullptr, err, s);
+    case 16: return launch_typed<T, 16, 128, 8, false, false, RAW>(p, split, nullptr, err, s);
+    case 32: return launch_typed<T, 32, 128, 8, false, false, RAW>(p, split, nullptr, err, s);
+    case 64: return launch_typed<T, 64, 128, 6, false, false, RAW>(p, split, nullptr, err, s);
+    case 128: return launch_typed<T, 128, 128, 4, false, false, RAW>(p, split, nullptr, err, s);
+    case 256: return launch_typed<T, 256, 128, 2, false, false, RAW>(p, split, nullptr, err, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+cudaError_t launch_raw_any(const Problem& p, int split, int tile_t, int tile_n, int stages, unsigned int* err,
+                           cudaStream_t s) {
+  switch (p.raw) {
+    case kRawW: return launch_raw<T, kRawW>(p, split, tile_t, tile_n, stages, err, s);
+    case kRawA: return launch_raw<T, kRawA>(p, split, tile_t, tile_n, stages, err, s);
+    case kRawW | kRawA: return launch_raw<T, kRawW | kRawA>(p, split, tile_t, tile_n, stages, err, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1023,10 +1259,10 @@ cudaError_t tc_prepare_device() {
 
 cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
                       const Gather* g, unsigned int* err, cudaStream_t s) {
-  if (p.w_ldg) {
+  if (p.raw != 0) {
     if (g != nullptr || w_mn) return cudaErrorInvalidValue;
-    return p.dtype == GLQ_DTYPE_BF16 ? launch_ldg<__nv_bfloat16>(p, split, tile_t, tile_n, stages, err, s)
-                                     : launch_ldg<__half>(p, split, tile_t, tile_n, stages, err, s);
+    return p.dtype == GLQ_DTYPE_BF16 ? launch_raw_any<__nv_bfloat16>(p, split, tile_t, tile_n, stages, err, s)
+                                     : launch_raw_any<__half>(p, split, tile_t, tile_n, stages, err, s);
   }
   if (g != nullptr) {
     if (p.dtype == GLQ_DTYPE_BF16) {

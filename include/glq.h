@@ -76,10 +76,11 @@ enum glq_path {
   GLQ_PATH_REPACKED = 9,  /* strided or unaligned operands copied into the
                              caller's workspace with 16-B aligned rows, then
                              the tcgen05 or GEMV kernel on the copies */
-  GLQ_PATH_TC_LDG = 10,    /* no repack workspace, K-contiguous W rows not
-                             16-B aligned (odd K, pitch or base), A
-                             addressable: tcgen05 GEMM whose W stages the SM
-                             fills with plain loads */
+  GLQ_PATH_TC_LDG = 10,   /* K-contiguous A or W rows not 16-B aligned (odd
+                             K, pitch or base), W = B^T K-contiguous:
+                             tcgen05 GEMM that loads those rows by row class
+                             with TMA and aligns them in shared memory (no
+                             copy, no workspace) */
   GLQ_PATH_COUNT = 11
 };
 
@@ -212,12 +213,15 @@ size_t glq_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k);
  * 16-byte aligned, overlapping rows, or no unit stride) is first copied into
  * the workspace with 16-byte aligned rows, and the call then runs the
  * tcgen05 or GEMV kernel on the copies (path GLQ_PATH_REPACKED).  0 when
- * the operands are addressable as they are.  Given less, such a call runs
- * the generic kernel (GLQ_PATH_STRIDED / GLQ_PATH_UNALIGNED) or, for a
- * K-contiguous W with an addressable A, the tcgen05 kernel with W loaded by
- * the SM (GLQ_PATH_TC_LDG), as it does when the workspace is not 16-byte
- * aligned.  When the
- * workspace serves a repack it holds no split partials.  Pure host function.
+ * the operands are addressable as they are, and when the tcgen05 kernel
+ * aligns them itself (K-contiguous rows of A and of W = B^T whose base or
+ * pitch is off 16 bytes, at most 128 tokens: GLQ_PATH_TC_LDG, no copy; above
+ * 128 tokens such operands are copied when the workspace allows, since every
+ * token tile would re-align the same weight tiles).  Given less, such a call
+ * runs the generic kernel (GLQ_PATH_STRIDED / GLQ_PATH_UNALIGNED), or
+ * GLQ_PATH_TC_LDG for those K-contiguous rows, as it does when the workspace
+ * is not 16-byte aligned.  When the workspace
+ * serves a repack it holds no split partials.  Pure host function.
  * No counterpart in the reference: the lab's Triton kernel reads any
  * contiguous layout through masked loads (kernels.py:103-129) and sends
  * strided views to torch (qualification.py:58-64).

@@ -73,8 +73,10 @@ def test_plan_boundaries():
     assert plan(32, 0, 4096)[0] == "empty"
     assert plan(32, 4096, 0)[0] == "zero_k"
     assert plan(32, 4093, 4096)[0] == "tail"
-    # K = 4090 contiguous: row pitch 8180 B is not a multiple of 16 -> no TMA.
-    assert plan(32, 4096, 4090)[0] == "unaligned"
+    # K = 4090 contiguous: row pitch 8180 B is not a multiple of 16, so
+    # neither operand is a TMA source as it is; the tcgen05 kernel loads both
+    # by row class and aligns them in shared memory.
+    assert plan(32, 4096, 4090) == ("tc_ldg", 8)
     # K = 4090 in rows padded to 4096 elements: TMA with OOB zero fill.
     assert plan(32, 4096, 4090, a_strides=(4096, 1), b_strides=(1, 4096))[0] == "tail"
     # padded rows (K + 8) keep 16-byte pitches.
@@ -93,15 +95,18 @@ def test_plan_boundaries():
     assert plan(32, 4093, 4096, b_strides=(4093, 1))[0] == "unaligned"
     # neither operand dimension contiguous -> generic kernel.
     assert plan(32, 4096, 4096, b_strides=(2, 8192))[0] == "strided"
-    # base one element off 16-byte alignment.
-    assert plan(32, 4096, 4096, a_ptr=2)[0] == "unaligned"
-    # K-contiguous W rows that TMA cannot address with an addressable A: the
-    # tcgen05 kernel loads W by the SM (odd base, pitch or K) when the call
-    # has no repack workspace (what glq_plan plans).
+    # K-contiguous rows that TMA cannot address (odd base, pitch or K) in A,
+    # W or both: the tcgen05 kernel stages them raw and aligns them.
+    assert plan(32, 4096, 4096, a_ptr=2) == ("tc_ldg", 8)
     assert plan(1, 4096, 4096, b_ptr=2)[0] == "tc_ldg"
     assert plan(32, 4096, 4090, a_strides=(4096, 1)) == ("tc_ldg", 8)
     assert plan(32, 4096, 4096, b_strides=(1, 4100)) == ("tc_ldg", 8)
     assert plan(128, 4096, 4096, b_strides=(1, 4097)) == ("tc_ldg", 4)
+    assert plan(509, 4099, 4103)[0] == "tc_ldg"
+    # rows so short that 8 row classes cannot keep them apart (C * pitch must
+    # reach K + 8) leave the tensor-core path.
+    assert plan(4096, 4096, 1, a_strides=(1, 1), b_strides=(1, 1))[0] == "unaligned"
+    assert plan(4096, 4096, 3, a_strides=(3, 1), b_strides=(1, 3))[0] == "tc_ldg"
 
 
 @pytest.mark.parametrize("m", [1, 8, 32])
@@ -179,12 +184,21 @@ def test_linear_workspace_bytes():
     assert repack_bytes(32, 4096, 4096) == 0
     assert repack_bytes(32, 4096, 4096, b_strides=(4096, 1)) == 0
     assert repack_bytes(32, 4096, 4090, a_strides=(4096, 1), b_strides=(1, 4096)) == 0
-    # K = 4090 contiguous: both row pitches (8180 B) are unaligned.
-    assert repack_bytes(32, 4096, 4090) == padded(32, 4090) + padded(4096, 4090)
-    # only the operand that is off: a base two bytes off, a transposed A.
-    assert repack_bytes(32, 4096, 4096, a_ptr=2) == padded(32, 4096)
-    assert repack_bytes(1, 4096, 4096, b_ptr=2) == padded(4096, 4096)
+    # K-contiguous rows off 16 bytes (K = 4090 contiguous, a base two bytes
+    # off) in A or in W = B^T: the tcgen05 kernel aligns them itself, no copy.
+    assert repack_bytes(32, 4096, 4090) == 0
+    assert repack_bytes(32, 4096, 4096, a_ptr=2) == 0
+    assert repack_bytes(1, 4096, 4096, b_ptr=2) == 0
+    # above 128 tokens they are copied when the workspace allows (every token
+    # tile would re-align the same W tiles).
+    assert repack_bytes(509, 4099, 4103) == padded(509, 4103) + padded(4099, 4103)
+    assert repack_bytes(129, 4096, 4096, a_ptr=2) == padded(129, 4096)
+    assert repack_bytes(128, 4096, 4096, a_ptr=2) == 0
+    # a transposed A (no unit stride) is copied, and only A.
     assert repack_bytes(32, 4096, 4096, a_strides=(1, 32)) == padded(32, 4096)
+    # with a transposed A, a misaligned W is copied too (the copies then run
+    # the TMA kernels).
+    assert repack_bytes(32, 4096, 4090, a_strides=(1, 32)) == padded(32, 4090) + padded(4096, 4090)
     # B = [K, N] with N = 4093: the copy keeps B N-contiguous ([K, N] rows).
     assert repack_bytes(32, 4093, 4096, b_strides=(4093, 1)) == padded(4096, 4093)
     # no unit stride in B: copied K-contiguous.
@@ -195,7 +209,7 @@ def test_linear_workspace_bytes():
     # tail) run the small kernel on the operands as they are: no copy.
     assert repack_bytes(17, 257, 131, b_strides=(257, 1)) == 0
     assert repack_bytes(1, 4096, 1023) == 0
-    assert repack_bytes(1, 4096, 1025) == padded(4096, 1025)
+    assert repack_bytes(1, 4096, 1025) == 0
     assert repack_bytes(1, 4093, 4096, b_strides=(4093, 1)) == padded(4096, 4093)
     # nothing to compute, or invalid arguments.
     assert repack_bytes(0, 4096, 4090) == 0
@@ -400,58 +414,87 @@ def test_gather_static_validates_before_touching_its_slot():
     assert call(epoch=0) == 1
 
 
-def ldg_stage_image(mem: bytes, base: int, pitch: int, n_rows: int, k: int, k0: int) -> bytes:
-    """Host restatement of one 128-row x 64-K W stage written by the tc_ldg
-    producer (warps 2..5): lane t of the 128 producer threads owns chunk
-    c = t % 8 of rows t / 8 + 16 j; lo = the aligned granule holding the
-    chunk's first byte (read if it starts before the row's end), hi = the
-    next lane's lo, or, for c = 7, its own load of the next granule; the
-    32-byte window is shifted by the row's byte offset, columns >= K and rows
-    >= N are zero, and chunk c of row r lands at r * 128 + (c ^ (r % 8)) * 16.
-    `mem` holds the bytes at addresses 0 .. len(mem)."""
-    stage = bytearray(128 * 128)
-    g16 = lambda addr: mem[addr:addr + 16] if addr + 16 <= len(mem) else bytes(16)
-    for t in range(128):
-        c = t % 8
-        for j in range(8):
-            r = t // 8 + 16 * j
-            out = bytes(16)
-            if r < n_rows and k - (k0 + 8 * c) > 0:
-                row_begin = base + r * pitch
-                row_end = row_begin + 2 * k
-                first = row_begin + 2 * k0
-                g = (first & ~15) + 16 * c
-                shift = first & 15
-                lo = g16(g) if g < row_end else bytes(16)
-                if c == 7:
-                    hi = g16(g + 16) if shift and g + 16 < row_end else bytes(16)
-                else:
-                    hi = g16(g + 16) if g + 16 < row_end else bytes(16)  # the next lane's lo
-                window = lo + hi
-                out = bytearray(window[shift:shift + 16])
-                valid = k - (k0 + 8 * c)
-                for e in range(8):
-                    if e >= valid:
-                        out[2 * e:2 * e + 2] = b"\0\0"
-                out = bytes(out)
-            off = r * 128 + ((c ^ (r % 8)) * 16)
-            stage[off:off + 16] = out
+def raw_classes(base: int, rows: int, k: int, pitch: int):
+    """Row classes of a raw-staged operand, as the library plans them: the
+    smallest power of two C <= 8 with C * pitch a multiple of 8 elements and
+    C * pitch >= k + 8; per class c the element offset s_c of its first row
+    inside a 16-byte granule, and that granule's byte address."""
+    pe = (k + 15) // 8 * 8 if rows <= 1 else pitch
+    c = 1 if pe % 8 == 0 else 2 if pe % 4 == 0 else 4 if pe % 2 == 0 else 8
+    while c < 8 and c * pe < k + 8:
+        c *= 2
+    if c * pe < k + 8:
+        return None
+    b0 = (base & 15) // 2
+    classes = []
+    for i in range(c):
+        e = b0 + i * pe
+        classes.append({"s": e & 7, "origin": (base & ~15) + 2 * (e - (e & 7)),
+                        "rows": max(0, (rows - i + c - 1) // c)})
+    return c, pe, classes
+
+
+def raw_stage_image(mem: bytes, base: int, pitch: int, n_rows: int, k: int, k0: int, tile_rows: int = 128) -> bytes:
+    """Host restatement of one stage of a raw-staged operand.
+
+    TMA side: per row class c, one box of (tile_rows / C) rows x 72 elements
+    at x = k0 of a map whose rows are class rows (pitch C * pitch elements,
+    origin the granule below the class's first row), inner extent k + s_c,
+    zero outside the map.  Shift side: chunk g of tile row r (class c = r % C,
+    class row i = r / C) is raw granules g and g + 1 of that raw row, shifted
+    by s_c elements, written at r * 128 + (g ^ (r % 8)) * 16.  The shift
+    warps visit the rows in class order, four rows per warp step; every
+    (row, chunk) is written once.  Class c's box lands c slots
+    in, a slot being (tile_rows / C) * 144 bytes rounded up to 128.  `mem`
+    holds the bytes at addresses 0 .. len(mem)."""
+    c_count, pe, classes = raw_classes(base, n_rows, k, pitch)
+    per = tile_rows // c_count
+    # class c's box starts c slots in: per * 144 bytes rounded up to 128
+    box = [c * (-(-per * 144 // 128) * 128) for c in range(c_count)]
+    raw = bytearray(box[-1] + per * 144 + 32)
+    for c, cl in enumerate(classes):
+        for i in range(per):
+            if i >= cl["rows"]:
+                continue
+            for x in range(k0, k0 + 72):
+                if x < k + cl["s"]:
+                    addr = cl["origin"] + 2 * (i * c_count * pe + x)
+                    off = box[c] + i * 144 + 2 * (x - k0)
+                    raw[off:off + 2] = mem[addr:addr + 2]
+    stage = bytearray(tile_rows * 128)
+    written = set()
+    log_c = c_count.bit_length() - 1
+    rpc = tile_rows // c_count
+    for u in range(tile_rows // 4):  # warp steps (contiguous blocks per shift warp)
+        for lane in range(32):
+            idx = 4 * u + lane // 8
+            g = lane % 8
+            c, i = idx // rpc, idx % rpc
+            r = (i << log_c) + c
+            s = classes[c]["s"]
+            row = box[c] + i * 144 + 16 * g
+            window = bytes(raw[row: row + 32])
+            off = r * 128 + ((g ^ (r % 8)) * 16)
+            stage[off:off + 16] = window[2 * s: 2 * s + 16]
+            written.add((r, g))
+    assert len(written) == tile_rows * 8
     return bytes(stage)
 
 
-@pytest.mark.parametrize("k,pitch,base", [(4090, 4090, 64), (4096, 4098, 128), (4096, 4096, 130), (1001, 1001, 70),
-                                          (131, 135, 2)])
-def test_ldg_stage_restatement(k, pitch, base):
-    """The producer's granule / shuffle / shift mapping and its swizzle
-    placement give exactly the 128-byte-swizzled K-major tile of the rows
-    (what a TMA load with out-of-bounds zero fill would write)."""
-    rng = np.random.default_rng(k + pitch + base)
-    n_rows = 100  # ragged: rows >= N are zero
-    mem = rng.integers(0, 256, size=base + n_rows * pitch * 2 + 64, dtype=np.uint8).tobytes()
+@pytest.mark.parametrize("k,pitch,base,rows", [(4090, 4090, 64, 100), (4096, 4098, 128, 100), (4096, 4096, 130, 100),
+                                               (1001, 1001, 70, 100), (131, 135, 2, 100), (4096, 4096, 2, 1),
+                                               (4090, 4090, 6, 32), (200, 201, 14, 3), (1001, 1001, 2, 16)])
+def test_raw_stage_restatement(k, pitch, base, rows):
+    """Row-class boxes plus the in-shared-memory shift give exactly the
+    128-byte-swizzled K-major tile of the rows: what a TMA load with zero
+    fill writes from an aligned copy (rows >= N and columns >= K zero)."""
+    rng = np.random.default_rng(k + pitch + base + rows)
+    mem = rng.integers(0, 256, size=base + rows * pitch * 2 + 64, dtype=np.uint8).tobytes()
+    tile_rows = 128 if rows > 32 else 32 if rows > 16 else 16
     for k0 in range(0, k, 64 * max(1, k // 256)):
-        got = ldg_stage_image(mem, base, pitch * 2, n_rows, k, k0)
-        want = bytearray(128 * 128)
-        for r in range(min(n_rows, 128)):
+        got = raw_stage_image(mem, base, pitch, rows, k, k0, tile_rows)
+        want = bytearray(tile_rows * 128)
+        for r in range(min(rows, tile_rows)):
             row = mem[base + r * pitch * 2 + 2 * k0: base + r * pitch * 2 + 2 * min(k, k0 + 64)]
             dense = row + bytes(128 - len(row))
             for off in range(0, 128, 16):
@@ -459,3 +502,25 @@ def test_ldg_stage_restatement(k, pitch, base):
                 swz = linear ^ (((linear >> 7) & 7) << 4)  # 128-byte swizzle: bits 4-6 ^= bits 7-9
                 want[swz:swz + 16] = dense[off:off + 16]
         assert got == bytes(want), f"k0={k0}"
+
+
+def test_raw_class_maps_stay_inside_the_operand():
+    """Every byte a class map can read (its rows x (k + s_c) elements from its
+    origin) lies inside the 16-byte granules that hold the operand's rows,
+    and the class rows do not overlap."""
+    for base, rows, k, pitch in [(2, 4096, 4090, 4090), (66, 33, 1001, 1003), (130, 7, 4096, 4096),
+                                 (14, 1, 77, 77), (6, 100, 131, 135)]:
+        c_count, pe, classes = raw_classes(base, rows, k, pitch)
+        assert (c_count * pe) % 8 == 0 and c_count * pe >= k + 8
+        first = base & ~15
+        last = (base + 2 * ((rows - 1) * pitch + k) + 15) & ~15
+        for c, cl in enumerate(classes):
+            assert cl["origin"] % 16 == 0
+            if cl["rows"]:
+                lo = cl["origin"]
+                hi = cl["origin"] + 2 * ((cl["rows"] - 1) * c_count * pe + k + cl["s"])
+                assert first <= lo and hi <= last
+                # row i of the class starts at the class row's element s_c
+                for i in range(cl["rows"]):
+                    r = c + c_count * i
+                    assert cl["origin"] + 2 * (i * c_count * pe + cl["s"]) == base + 2 * r * pitch

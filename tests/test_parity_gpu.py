@@ -194,11 +194,12 @@ def probe_inputs(probe, device):
     return a, w, bias, da, dw, bias.to(device)
 
 
-# The operator API gives the library a workspace for operands the TMA
-# kernels cannot address, so those probes take the repacked path.
-EXPECTED_PROBE_PATH = {"zero-m": "empty", "zero-k": "zero_k", "tail-n": "tail", "tail-k": "repacked",
+# K-contiguous rows off 16 bytes (tail K = 4090, a base one element off) run
+# the tcgen05 kernel that aligns them itself; a transposed A (no unit stride)
+# is copied into the workspace the operator API provides.
+EXPECTED_PROBE_PATH = {"zero-m": "empty", "zero-k": "zero_k", "tail-n": "tail", "tail-k": "tc_ldg",
                        "a-row-stride": "tc_splitk", "w-row-stride": "tc_splitk",
-                       "a-transposed": "repacked", "misaligned-base": "repacked"}
+                       "a-transposed": "repacked", "misaligned-base": "tc_ldg"}
 
 
 @pytest.mark.parametrize("probe", workloads.MANIFEST["probes"], ids=[p["id"] for p in workloads.MANIFEST["probes"]])
@@ -229,13 +230,12 @@ def aligned_copy(x: torch.Tensor, device) -> torch.Tensor:
 # (id, M, N, K, A layout, B layout); B layouts: "w_nk" = W[N, K].T, "b_kn" =
 # B[K, N] row-major, "w_strided" = W[N, K].T with neither stride unit.
 REPACK_CASES = [
-    ("k4090", 32, 4096, 4090, "contiguous", "w_nk"),
-    ("m1-k4090", 1, 4096, 4090, "contiguous", "w_nk"),
     ("k131-wide", 64, 2055, 131, "contiguous", "b_kn"),
     ("n4093-b_kn", 32, 4093, 4096, "contiguous", "b_kn"),
     ("m1-n4093-b_kn", 1, 4093, 4096, "contiguous", "b_kn"),
-    ("a-offset", 32, 4096, 4096, "offset", "w_nk"),
     ("a-transposed", 32, 4096, 4096, "transposed", "w_nk"),
+    ("a-transposed-k4090", 32, 4096, 4090, "transposed", "w_nk"),
+    ("m509-k4103", 509, 4099, 4103, "contiguous", "w_nk"),
     ("w-strided", 8, 2048, 520, "contiguous", "w_strided"),
     ("m129-odd", 129, 1031, 65, "contiguous", "b_kn"),
 ]
@@ -257,12 +257,12 @@ def layout_operands(case, dtype, device):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
 @pytest.mark.parametrize("case", REPACK_CASES, ids=[c[0] for c in REPACK_CASES])
 def test_repacked_matches_aligned_copy(cuda_device, case, dtype):
-    """Strided or unaligned operands with a workspace: the repack kernel's
+    """Strided operands, unaligned ones in the lab's B = [K, N], and unaligned
+    K-contiguous ones above 128 tokens, with a workspace: the repack kernel's
     aligned copies go through the same tcgen05 / GEMV plan as operands that
     were aligned to begin with, so the bits equal that call's; without a
-    workspace the generic kernel runs (or, when only a K-contiguous W is
-    off, the tcgen05 kernel with W loaded by the SM).  Both pass the oracle
-    gate."""
+    workspace the generic kernel runs (or, for K-contiguous rows, the
+    tcgen05 kernel that aligns them itself).  Both pass the oracle gate."""
     _, m, n, k, _, b_layout = case
     a, w, bias, da, b = layout_operands(case, dtype, cuda_device)
     b_al = aligned_copy(w.t().contiguous(), cuda_device) if b_layout == "b_kn" else aligned_copy(w, cuda_device).t()
@@ -279,7 +279,7 @@ def test_repacked_matches_aligned_copy(cuda_device, case, dtype):
     out_generic = torch.empty((m, n), dtype=dtype, device=cuda_device)
     out_rep, out_al = torch.empty_like(out_generic), torch.empty_like(out_generic)
     path_g, split_g = native.linear(da, b, out_generic, db, epi)
-    # no workspace: the generic kernel, or the SM-loaded W when only W is off
+    # no workspace: the generic kernel, or the raw-staged tcgen05 kernel
     assert path_g in ("unaligned", "strided", "tc_ldg")
     path_r, split_r = native.linear(da, b, out_rep, db, epi, workspace=ws)
     assert path_r == "repacked"
@@ -341,68 +341,102 @@ def test_small_kernel(cuda_device, case, dtype):
     oracle.compare(host(plain), oracle.linear_reference(a, w, samples=8), atol, rtol)
 
 
-# Without a workspace: K-contiguous W rows that TMA cannot address (odd K,
-# a row pitch that is not a multiple of 8 elements, a base off 16 bytes)
-# with A in 16-byte-pitched rows.  (id, M, N, K, W row pitch in elements
-# (None: K), W base offset in elements).
-LDG_CASES = [
-    ("k4090", 32, 4096, 4090, None, 0),
-    ("m1-k4090", 1, 4096, 4090, None, 0),
-    ("w-pitch", 32, 4096, 4096, 4098, 0),
-    ("w-offset", 8, 4096, 4096, None, 1),
-    ("m129-k4090", 129, 1031, 4090, None, 0),
-    ("m256-ragged", 256, 777, 1001, None, 0),
+# K-contiguous rows that TMA cannot address as they are (odd K, a row pitch
+# that is not a multiple of 8 elements, a base off 16 bytes), in A, in W or
+# in both: the tcgen05 kernel loads them by row class and aligns them in
+# shared memory.  (id, M, N, K, A pitch, A offset, W pitch, W offset), pitches
+# in elements (None: K rounded up to 8, i.e. an aligned operand), offsets in
+# elements from a 256-byte aligned allocation.
+RAW_CASES = [
+    ("k4090-both", 32, 4096, 4090, 4090, 0, 4090, 0),
+    ("k4090-w", 32, 4096, 4090, None, 0, 4090, 0),
+    ("a-offset", 32, 4096, 4096, 4096, 1, None, 0),
+    ("a-pitch-odd", 8, 4096, 4096, 4097, 0, None, 0),
+    ("w-pitch4100", 32, 4096, 4096, None, 0, 4100, 0),
+    ("w-offset", 8, 4096, 4096, None, 0, 4096, 1),
+    ("both-offset", 16, 2048, 1000, 1000, 3, 1000, 5),
+    ("m1-k4090", 1, 4096, 4090, 4090, 0, 4090, 0),
+    ("m64-k4095", 64, 2048, 4095, 4095, 0, 4095, 0),
+    ("k4095-a8-classes", 32, 4096, 4095, 4095, 0, 4095, 0),
+    ("m16-k4095-a8-classes", 16, 2048, 4095, 4095, 0, 4095, 0),
+    ("m128-k4090", 128, 4096, 4090, 4090, 0, 4090, 0),
+    ("m129-k4090", 129, 1031, 4090, 4090, 0, 4090, 0),
+    ("m256-ragged", 256, 777, 1001, 1001, 0, 1001, 0),
+    ("m509-odd", 509, 4099, 4103, 4103, 0, 4103, 0),
 ]
 
 
+def placed(x: torch.Tensor, pitch, offset: int, device):
+    """x ([rows, k]) at `offset` elements into NaN storage, rows `pitch`
+    elements apart; returns (storage, view, first element, end element)."""
+    rows, k = x.shape
+    pitch = -(-k // 8) * 8 if pitch is None else pitch
+    store = torch.full((rows * pitch + offset + 64,), float("nan"), dtype=x.dtype, device=device)
+    view = store[offset:offset + rows * pitch].view(rows, pitch)[:, :k]
+    view.copy_(x.to(device))
+    return store, view, offset, offset + (rows - 1) * pitch + k
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
-@pytest.mark.parametrize("case", LDG_CASES, ids=[c[0] for c in LDG_CASES])
-def test_sm_loaded_w_matches_aligned_copy(cuda_device, case, dtype):
-    """With no workspace, the tcgen05 kernel with W written into its stages
-    by the SM (path tc_ldg) gives the bits of the same plan on
-    16-byte-pitched copies."""
-    _, m, n, k, pitch, offset = case
+@pytest.mark.parametrize("case", RAW_CASES, ids=[c[0] for c in RAW_CASES])
+def test_raw_staged_matches_aligned_copy(cuda_device, case, dtype):
+    """The tcgen05 kernel on operands it stages raw and aligns itself (path
+    tc_ldg, called without a workspace) gives the bits of the same plan on
+    16-byte-pitched copies, passes the oracle gate, and reads and writes nothing outside
+    the operands (NaN storage around them stays NaN, and no NaN reaches Y)."""
+    _, m, n, k, a_pitch, a_off, w_pitch, w_off = case
     a, w, bias = workloads.uniform_inputs(m, n, k, dtype=dtype)
-    pitch = k if pitch is None else pitch
-    store = torch.full((n * pitch + offset + 64,), float("nan"), dtype=dtype, device=cuda_device)
-    dw = store[offset:offset + n * pitch].view(n, pitch)[:, :k]
-    dw.copy_(w.to(cuda_device))
-    da, db = aligned_copy(a, cuda_device), bias.to(cuda_device)
+    a_store, da, a_lo, a_hi = placed(a, a_pitch, a_off, cuda_device)
+    w_store, dw, w_lo, w_hi = placed(w, w_pitch, w_off, cuda_device)
+    db = bias.to(cuda_device)
     code = native.dtype_code(dtype)
     need = native.linear_workspace_bytes(code, da.data_ptr(), da.stride(), dw.data_ptr(), dw.t().stride(), m, n, k)
-    # a repack workspace would hold the W copy alone (A is addressable); this
-    # call gets none, so W is loaded by the SM
-    assert need == -(-n * (-(-k // 8) * 8) * 2 // 256) * 256
+    # up to 128 tokens no copy is wanted; above, a caller's workspace would
+    # hold copies (this call gives none)
+    assert (need == 0) == (m <= 128)
     epi = native.EPILOGUE_BIAS_SILU
     out = torch.empty((m, n), dtype=dtype, device=cuda_device)
     out_al = torch.empty_like(out)
     path, split = native.linear(da, dw.t(), out, db, epi)
     assert path == "tc_ldg"
     if m > 1:
-        path_al, split_al = native.linear(da, aligned_copy(w, cuda_device).t(), out_al, db, epi)
+        path_al, split_al = native.linear(aligned_copy(a, cuda_device), aligned_copy(w, cuda_device).t(), out_al,
+                                          db, epi)
         assert path_al not in ("unaligned", "repacked", "tc_ldg") and split == split_al
     else:
         # M = 1 on aligned rows is a GEMV: check that the call repeats its bits.
         native.linear(da, dw.t(), out_al, db, epi)
     torch.cuda.synchronize()
     assert torch.equal(out.view(torch.int16), out_al.view(torch.int16))
+    assert not torch.isnan(out).any()
     atol, rtol = (U_ATOL, U_RTOL) if dtype == torch.float16 else (0.05, 0.01)
     oracle.compare(host(out), oracle.linear_reference(a, w, bias, silu=True, samples=8), atol, rtol)
-    # the storage around W is untouched NaN: nothing was written there
-    assert torch.isnan(store[:offset]).all() and torch.isnan(store[offset + n * pitch:]).all()
+    plain = torch.empty_like(out)
+    native.linear(da, dw.t(), plain, None, native.EPILOGUE_NONE)
+    oracle.compare(host(plain), oracle.linear_reference(a, w, samples=8), atol, rtol)
+    for store, lo, hi in ((a_store, a_lo, a_hi), (w_store, w_lo, w_hi)):
+        assert torch.isnan(store[:lo]).all() and torch.isnan(store[hi:]).all()
 
 
-def test_repacked_fused_chain_in_a_graph(cuda_device):
-    """Repacked calls (the workspace comes from torch's caching allocator
-    inside the capture) replay bit-exactly from a CUDA graph."""
+@pytest.mark.parametrize("a_layout,path", [("contiguous", "tc_ldg"), ("transposed", "repacked")])
+def test_unaligned_fused_chain_in_a_graph(cuda_device, a_layout, path):
+    """Chains of calls on operands TMA cannot address as they are replay
+    bit-exactly from a CUDA graph: K = 4090 rows aligned inside the kernel,
+    and repacked calls whose workspace comes from torch's caching allocator
+    inside the capture."""
     a, w, bias = workloads.uniform_inputs(32, 4090, 4090)
-    da, dw, db = a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    da = a.to(cuda_device) if a_layout == "contiguous" else workloads.poisoned_view(a, "transposed", cuda_device)
+    dw, db = w.to(cuda_device), bias.to(cuda_device)
     y1 = torch.empty((32, 4090), dtype=torch.float16, device=cuda_device)
     y2 = torch.empty_like(y1)
 
+    paths = []
+
     def chain():
         kernels.triton_bias_silu_into(da, dw.t(), db, y1)
+        paths.append(kernels.last_path()[0])
         kernels.triton_bias_silu_into(y1, dw.t(), db, y2)
+        paths.append(kernels.last_path()[0])
 
     side = torch.cuda.Stream(cuda_device)
     side.wait_stream(torch.cuda.current_stream())
@@ -410,7 +444,8 @@ def test_repacked_fused_chain_in_a_graph(cuda_device):
         chain()
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
-    assert kernels.last_path()[0] == "repacked"
+    # the second call reads the first one's contiguous K = 4090 output
+    assert paths == [path, "tc_ldg"]
     eager = y2.clone()
     oracle.compare(host(y1), oracle.linear_reference(a, w, bias, silu=True, samples=8), U_ATOL, U_RTOL)
     graph = torch.cuda.CUDAGraph()
