@@ -204,6 +204,12 @@ Problem repacked_problem(const Problem& p, const RepackPlan& r, void* workspace)
     // The copy is written by the kernel just before: the GEMM must not read
     // W ahead of its grid-dependency wait.
     q.flags &= ~static_cast<unsigned int>(GLQ_FLAG_STATIC_WEIGHTS);
+  } else if (r.a) {
+    // Only A is copied.  W is not written by the copy kernel, and the copy
+    // kernel waits for its own predecessor before it lets the GEMM launch, so
+    // the GEMM may stream W before its dependency wait (as with static
+    // weights): the weight stream overlaps the copy of A.
+    q.flags |= static_cast<unsigned int>(GLQ_FLAG_STATIC_WEIGHTS);
   }
   return q;
 }

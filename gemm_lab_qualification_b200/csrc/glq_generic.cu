@@ -14,7 +14,8 @@
 // (kernels.py:143-144); strided views fell back to torch there
 // (qualification.py:58-64).
 //
-// fill_kernel: K = 0 makes every sum empty, so Y = epilogue(0 [+ bias]).
+// fill_kernel: K = 0 makes every sum empty, so Y = epilogue(0 [+ bias]),
+// the same row M times: one value per column chunk, stored down the rows.
 //
 // repack_rows_kernel / repack_strided_kernel: with a caller workspace, an
 // operand the TMA kernels cannot address (row pitch or base not 16-byte
@@ -167,14 +168,30 @@ __global__ void __launch_bounds__(kThreads) generic_kernel(const GenericArgs g) 
   }
 }
 
-template <typename T>
-__global__ void fill_kernel(T* y, long long ldy, long long m, long long n, const T* bias, int epilogue) {
-  const long long total = m * n;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / n, c = i % n;
-    const float bias_v = epilogue != GLQ_EPILOGUE_NONE ? Conv<T>::to_f(bias[c]) : 0.0f;
-    y[r * ldy + c] = Conv<T>::from_f(apply_epilogue(0.0f, bias_v, epilogue));
+// Every row of the result is the same: thread x of block (bx, by) owns the
+// column chunk bx * 256 + x (8 columns, one 16-byte store per row when
+// VEC, else one column) and stores it to rows by, by + gridDim.y, ...
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) fill_kernel(T* y, long long ldy, long long m, long long n, const T* bias,
+                                                   int epilogue) {
+  // The bias may be written by the previous kernel in the stream.
+  ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
+  constexpr int kCols = VEC ? 8 : 1;
+  const long long c0 = (static_cast<long long>(blockIdx.x) * 256 + threadIdx.x) * kCols;
+  if (c0 >= n) return;
+  T v[kCols];
+#pragma unroll
+  for (int j = 0; j < kCols; ++j) {
+    const float bias_v = epilogue != GLQ_EPILOGUE_NONE ? Conv<T>::to_f(bias[c0 + j]) : 0.0f;
+    v[j] = Conv<T>::from_f(apply_epilogue(0.0f, bias_v, epilogue));
+  }
+  for (long long r = blockIdx.y; r < m; r += gridDim.y) {
+    if constexpr (VEC) {
+      *reinterpret_cast<uint4*>(y + r * ldy + c0) = *reinterpret_cast<const uint4*>(v);
+    } else {
+      y[r * ldy + c0] = v[0];
+    }
   }
 }
 
@@ -405,20 +422,33 @@ cudaError_t launch_repack(const void* src, int64_t rows, int64_t cols, int64_t r
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_fill_typed(const Problem& p, cudaStream_t s) {
+  // 16-byte stores when every row's chunk is 16-byte aligned.
+  const bool vec = p.n % 8 == 0 && p.ldy % 8 == 0 && reinterpret_cast<uintptr_t>(p.y) % 16 == 0;
+  const long long chunks = vec ? p.n / 8 : p.n;
+  const long long col_blocks = (chunks + 255) / 256;
+  // About two CTAs per SM in all; rows beyond gridDim.y loop.
+  const long long row_blocks = std::max<long long>(1, std::min<long long>({p.m, 65535, (296 + col_blocks - 1) / col_blocks}));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(col_blocks), static_cast<unsigned>(row_blocks), 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 0 : 1;
+  T* y = static_cast<T*>(p.y);
+  const T* bias = static_cast<const T*>(p.bias);
+  return vec ? cudaLaunchKernelEx(&cfg, fill_kernel<T, true>, y, static_cast<long long>(p.ldy), static_cast<long long>(p.m),
+                                  static_cast<long long>(p.n), bias, p.epilogue)
+             : cudaLaunchKernelEx(&cfg, fill_kernel<T, false>, y, static_cast<long long>(p.ldy),
+                                  static_cast<long long>(p.m), static_cast<long long>(p.n), bias, p.epilogue);
+}
+
 cudaError_t launch_fill(const Problem& p, cudaStream_t s) {
-  const long long total = p.m * p.n;
-  long long blocks = (total + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  if (blocks < 1) blocks = 1;
-  if (p.dtype == GLQ_DTYPE_BF16) {
-    fill_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        static_cast<__nv_bfloat16*>(p.y), p.ldy, p.m, p.n, static_cast<const __nv_bfloat16*>(p.bias),
-        p.epilogue);
-  } else {
-    fill_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        static_cast<__half*>(p.y), p.ldy, p.m, p.n, static_cast<const __half*>(p.bias), p.epilogue);
-  }
-  return cudaGetLastError();
+  return p.dtype == GLQ_DTYPE_BF16 ? launch_fill_typed<__nv_bfloat16>(p, s) : launch_fill_typed<__half>(p, s);
 }
 
 }  // namespace glq

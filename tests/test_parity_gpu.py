@@ -176,6 +176,34 @@ def test_tcgen05_tails_in_padded_rows(cuda_device, m, n, k):
     assert_guard_intact(guard, m, n, pitch=pitch)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("m,n,pitch", [(32, 4096, 4096), (3, 4093, 4093), (70000, 16, 24), (5, 24, 31), (1, 8, 8)])
+def test_zero_k_fill(cuda_device, m, n, pitch, dtype):
+    """K = 0: every row is epilogue(0 + bias) (16-byte stores down the rows
+    when the rows allow, element stores otherwise); nothing outside Y is
+    written."""
+    g = torch.Generator().manual_seed(m + n)
+    bias = ((torch.rand((n,), generator=g) - 0.5) * 8).to(dtype)
+    da = torch.empty((m, 0), dtype=dtype, device=cuda_device)
+    db = torch.empty((0, n), dtype=dtype, device=cuda_device)
+    for fused in (True, False):
+        guard, out = guarded_output(m, n, dtype, cuda_device, pitch=pitch)
+        if fused:
+            kernels.triton_bias_silu_into(da, db, bias.to(cuda_device), out)
+        else:
+            kernels.triton_matmul_into(da, db, out)
+        assert kernels.last_path()[0] == "zero_k"
+        torch.cuda.synchronize()
+        assert_guard_intact(guard, m, n, pitch=pitch)
+        got = out.float().cpu()
+        if fused:
+            row = torch.nn.functional.silu(bias.float())
+            torch.testing.assert_close(got, row.expand(m, n), atol=1e-3, rtol=1e-2)
+            assert torch.equal(got, got[:1].expand(m, n)), "rows differ"
+        else:
+            assert torch.equal(got, torch.zeros((m, n)))
+
+
 # ------------------------------------------------------------------ boundary probes
 
 def probe_inputs(probe, device):
