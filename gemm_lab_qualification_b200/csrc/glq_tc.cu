@@ -166,15 +166,21 @@ struct TcConfig {
   static constexpr uint32_t kStageAlign = (kRawW_ && kRawA_) ? 128u : 1024u;
   static constexpr uint32_t kStageBytes = (kLoadWBytes + kLoadABytes + kStageAlign - 1u) / kStageAlign * kStageAlign;
   static constexpr int kStages = STAGES;
-  // Aligned stages of the RAW kernels (swizzled W if raw, then swizzled A if
-  // raw): two, so that the shift of stage i + 1 overlaps the MMA of stage i.
+  // Aligned stages of the RAW kernels: two, so that the shift of stage i + 1
+  // overlaps the MMA of stage i.  A raw W tile is aligned into tensor
+  // memory (the MMA's A operand: TMEM lane = tile row, 32 columns of two
+  // 16-bit elements per stage, past the accumulators); a raw A tile into
+  // a swizzled shared-memory stage.
   static constexpr int kShift = RAW == 0 ? 0 : 2;
-  static constexpr uint32_t kShiftAOffset = kRawW_ ? kWTileBytes : 0u;
-  static constexpr uint32_t kShiftBytes = (kRawW_ ? kWTileBytes : 0u) + (kRawA_ ? kATileBytes : 0u);
+  static constexpr uint32_t kShiftBytes = kRawA_ ? kATileBytes : 0u;
   static constexpr uint32_t kShiftBase = (kStages * kStageBytes + 1023u) / 1024u * 1024u;
   static constexpr uint32_t kAccCols = kAcc * BT;
+  static constexpr uint32_t kWTmemCol = (kAccCols + 31u) / 32u * 32u;  // first column of the W stages
+  static constexpr uint32_t kWTmemStageCols = kTileK / 2;               // 64 elements per row
+  static constexpr uint32_t kUsedCols = kRawW_ ? kWTmemCol + kShift * kWTmemStageCols : kAccCols;
   static constexpr uint32_t kTmemCols =
-      kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
+      kUsedCols <= 32 ? 32 : (kUsedCols <= 64 ? 64 : (kUsedCols <= 128 ? 128 : (kUsedCols <= 256 ? 256 : 512)));
+  static_assert(kUsedCols <= 512, "tensor memory holds 512 columns");
   static constexpr uint32_t kPipeBytes = kShiftBase + kShift * kShiftBytes;
   // full/empty per load stage, full/empty per aligned stage, done, receive.
   static constexpr int kBars = 2 * kStages + 2 * kShift + 2;
@@ -348,16 +354,85 @@ __device__ __forceinline__ void shift_rows(const uint8_t* raw, uint8_t* dst, int
   }
 }
 
+// Eight 16-byte chunks of one raw row (granules g and g + 1 for chunk g),
+// shifted by S elements, as the 32 TMEM columns of that row.
+template <int S>
+__device__ __forceinline__ void shift_row(const uint4 (&gr)[9], uint32_t (&lo)[16], uint32_t (&hi)[16]) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const uint4 v = shift_by<S>(gr[g], gr[g + 1]);
+    uint32_t* out = g < 4 ? lo + 4 * g : hi + 4 * (g - 4);
+    out[0] = v.x;
+    out[1] = v.y;
+    out[2] = v.z;
+    out[3] = v.w;
+  }
+}
+
+// A raw W load stage (TN = 128 rows) -> one aligned W stage in tensor
+// memory.  Lane l of the shift warp on TMEM sub-partition q = warp % 4
+// converts TMEM lane lam = 32 q + l, which holds row i of class c in
+// class-major order (lam = c * R + i, R = 128 / C rows per class), i.e.
+// tile row i * C + c: it loads that row's nine raw granules (consecutive
+// lanes read rows 144 B apart, free of bank conflicts), releases the load
+// stage once every lane has them, shifts them by the class's s_c and
+// writes the 64 elements as 32 TMEM columns of its lane.  With C <= 4 a
+// warp's 32 lanes share one class (a compile-time shift chosen once per
+// warp); with C = 8 the two half-warps shift by their own class's s_c.
+template <typename Release>
+__device__ __forceinline__ void shift_w_tmem(const uint8_t* raw, uint32_t tmem_stage, int classes, unsigned shifts,
+                                             Release release) {
+  const int q = (static_cast<int>(threadIdx.x) >> 5) & 3;
+  const int lane = threadIdx.x & 31;
+  const int lam = 32 * q + lane;
+  const int log_c = classes == 1 ? 0 : classes == 2 ? 1 : classes == 4 ? 2 : 3;
+  const int log_r = 7 - log_c;
+  const int c = lam >> log_r;
+  const int i = lam & ((1 << log_r) - 1);
+  const uint8_t* row = raw + raw_class_offset(c, 1 << log_r) + i * kRawRowBytes;
+  uint4 gr[9];
+#pragma unroll
+  for (int g = 0; g < 9; ++g) gr[g] = *reinterpret_cast<const uint4*>(row + 16 * g);
+  release();
+  const unsigned sh = (shifts >> (4 * c)) & 7u;
+  uint32_t lo[16], hi[16];
+  switch (sh) {
+    case 0: shift_row<0>(gr, lo, hi); break;
+    case 1: shift_row<1>(gr, lo, hi); break;
+    case 2: shift_row<2>(gr, lo, hi); break;
+    case 3: shift_row<3>(gr, lo, hi); break;
+    case 4: shift_row<4>(gr, lo, hi); break;
+    case 5: shift_row<5>(gr, lo, hi); break;
+    case 6: shift_row<6>(gr, lo, hi); break;
+    default: shift_row<7>(gr, lo, hi); break;
+  }
+  // The collective stores need the whole warp (the half-warps of C = 8 may
+  // have taken different cases above).
+  __syncwarp();
+  const uint32_t taddr = tmem_stage + (static_cast<uint32_t>(32 * q) << 16);
+  ptx::tmem_st_32x32b_x16(taddr, lo);
+  ptx::tmem_st_32x32b_x16(taddr + 16u, hi);
+}
+
+// Tile row of TMEM lane `lam` in a raw W tile (class-major lane order, see
+// shift_w_tmem).
+__device__ __forceinline__ int raw_w_tile_row(int lam, int classes) {
+  const int log_c = classes == 1 ? 0 : classes == 2 ? 1 : classes == 4 ? 2 : 3;
+  const int log_r = 7 - log_c;
+  return ((lam & ((1 << log_r) - 1)) << log_c) + (lam >> log_r);
+}
+
 // The shift warps' loop: for every K block of this CTA, wait for its load
-// stage and a free aligned stage, write the RAW operands' swizzled tiles,
-// release the load stage (one arrival per warp: the raw bytes are read) and
-// publish the aligned stage (every thread's writes made visible to the
-// tensor core by its own proxy fence, then one arrival per warp).
+// stage and a free aligned stage, write the RAW operands' aligned tiles (A
+// swizzled in shared memory, W in tensor memory), release the load stage
+// (one arrival per warp: the raw bytes are read) and publish the aligned
+// stage (every thread's writes made visible to the tensor core by its own
+// proxy fence or TMEM store wait, then one arrival per warp).
 template <int BT, int TN, int STAGES, int RAW, typename FullBar, typename EmptyBar, typename SFullBar,
           typename SEmptyBar, typename Raise>
-__device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, int nkb, FullBar full_bar,
-                                           EmptyBar empty_bar, SFullBar sfull_bar, SEmptyBar sempty_bar,
-                                           const volatile int* abort_flag, Raise raise) {
+__device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, uint32_t tmem_d, int nkb,
+                                           FullBar full_bar, EmptyBar empty_bar, SFullBar sfull_bar,
+                                           SEmptyBar sempty_bar, const volatile int* abort_flag, Raise raise) {
   using Cfg = TcConfig<BT, TN, STAGES, RAW>;
   const int lane = threadIdx.x & 31;
   for (int i = 0; i < nkb; ++i) {
@@ -376,6 +451,9 @@ __device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, in
       if (lane == 0) raise(kErrTimeoutProducer);
       return;
     }
+    // The MMAs that read this aligned stage have completed (their commit
+    // released sempty): order this warp's TMEM stores after them.
+    if constexpr (Cfg::kRawW_) ptx::tc_fence_after_sync();
     const uint8_t* load = smem + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
     uint8_t* aligned = smem + Cfg::kShiftBase + static_cast<uint32_t>(sst) * Cfg::kShiftBytes;
     // The load stage is released (one arrival per warp) once the last raw
@@ -387,16 +465,21 @@ __device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, in
     auto keep = []() {};
     if constexpr (Cfg::kRawA_) {
       if constexpr (Cfg::kRawW_) {
-        shift_rows<BT>(load + Cfg::kLoadWBytes, aligned + Cfg::kShiftAOffset, args.a_classes, args.a_shifts, keep);
+        shift_rows<BT>(load + Cfg::kLoadWBytes, aligned, args.a_classes, args.a_shifts, keep);
       } else {
-        shift_rows<BT>(load + Cfg::kLoadWBytes, aligned + Cfg::kShiftAOffset, args.a_classes, args.a_shifts,
-                       release);
+        shift_rows<BT>(load + Cfg::kLoadWBytes, aligned, args.a_classes, args.a_shifts, release);
       }
     }
-    if constexpr (Cfg::kRawW_) shift_rows<TN>(load, aligned, args.w_classes, args.w_shifts, release);
+    if constexpr (Cfg::kRawW_) {
+      static_assert(TN == 128, "raw W tiles are one M = 128 MMA");
+      shift_w_tmem(load, tmem_d + Cfg::kWTmemCol + static_cast<uint32_t>(sst) * Cfg::kWTmemStageCols,
+                   args.w_classes, args.w_shifts, release);
+      ptx::tmem_st_wait();
+      ptx::tc_fence_before_sync();
+    }
     // Every writer orders its stores before the tensor core's reads, then
     // one arrival per warp (128 arrivals on one barrier serialise).
-    ptx::fence_proxy_async_smem();
+    if constexpr (Cfg::kRawA_) ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(sfull_bar(sst));
   }
@@ -566,8 +649,14 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
   const int acc_idx = Cfg::kAcc == 2 ? half : 0;
   const int q_first = Cfg::kAcc == 2 ? 0 : half;
   const int q_step = Cfg::kAcc == 2 ? 1 : 2;
-  const int n_local = acc_idx * 128 + lane_group * 32 + lane;  // == threadIdx.x % TN
-  const long long n = static_cast<long long>(tile_n) * TN + n_local;
+  const int n_local = acc_idx * 128 + lane_group * 32 + lane;  // TMEM lane == threadIdx.x % TN
+  // The W row a TMEM lane holds: lane = tile row, except for a raw W tile
+  // (class-major lane order).  The split-K merge pairs partials by TMEM
+  // lane (every CTA of a cluster orders its rows the same way); the output
+  // and the bias use the W row.
+  int w_row = n_local;
+  if constexpr (Cfg::kRawW_) w_row = raw_w_tile_row(n_local, args.w_classes);
+  const long long n = static_cast<long long>(tile_n) * TN + w_row;
   const bool n_ok = n < args.n;
   float bias_v = 0.0f;
   if (args.epilogue != GLQ_EPILOGUE_NONE && n_ok) {
@@ -626,18 +715,26 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
         ptx::tc_fence_after_sync();
         const uint32_t load = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
         const uint32_t aligned = sbase + Cfg::kShiftBase + static_cast<uint32_t>(sst) * Cfg::kShiftBytes;
-        const uint32_t w_src = Cfg::kRawW_ ? aligned : load;
-        const uint32_t a_src = Cfg::kRawA_ ? aligned + Cfg::kShiftAOffset : load + Cfg::kLoadWBytes;
-        const uint64_t w_desc = WMN ? ptx::umma_desc_mn_sw128(w_src) : ptx::umma_desc_k_sw128(w_src);
+        const uint32_t a_src = Cfg::kRawA_ ? aligned : load + Cfg::kLoadWBytes;
         const uint64_t a_desc = ptx::umma_desc_k_sw128(a_src);
+        if constexpr (Cfg::kRawW_) {
+          // W from tensor memory: 8 columns (16 K elements) per MMA.
+          const uint32_t w_tmem = tmem_d + Cfg::kWTmemCol + static_cast<uint32_t>(sst) * Cfg::kWTmemStageCols;
 #pragma unroll
-        for (int kk = 0; kk < kTileK / 16; ++kk) {
-          // Each MMA consumes K = 16.  The 128-row halves of a 256-row W
-          // tile are 16 KB (1024 units) apart in both layouts.
+          for (int kk = 0; kk < kTileK / 16; ++kk) {
+            ptx::tc_mma_f16_ts(tmem_d, w_tmem + 8u * kk, a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        } else {
+          const uint64_t w_desc = WMN ? ptx::umma_desc_mn_sw128(load) : ptx::umma_desc_k_sw128(load);
 #pragma unroll
-          for (int h = 0; h < Cfg::kAcc; ++h) {
-            ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT), w_desc + 1024u * h + kWStep * kk,
-                            a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kTileK / 16; ++kk) {
+            // Each MMA consumes K = 16.  The 128-row halves of a 256-row W
+            // tile are 16 KB (1024 units) apart in both layouts.
+#pragma unroll
+            for (int h = 0; h < Cfg::kAcc; ++h) {
+              ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT), w_desc + 1024u * h + kWStep * kk,
+                              a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
         }
         if (kShift > 0) ptx::tc_commit(sempty_bar(sst));
@@ -647,8 +744,8 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
     }
   } else if (shifter) {
     if constexpr (RAW != 0) {
-      shift_loop<BT, TN, STAGES, RAW>(args, smem, nkb, full_bar, empty_bar, sfull_bar, sempty_bar, abort_flag,
-                                      raise);
+      shift_loop<BT, TN, STAGES, RAW>(args, smem, tmem_d, nkb, full_bar, empty_bar, sfull_bar, sempty_bar,
+                                      abort_flag, raise);
     }
   }
   __syncwarp();
@@ -1009,10 +1106,12 @@ bool encode_raw(CUtensorMap* maps, CUtensorMapDataType type, const void* base, i
   return true;
 }
 
-// Load-ring depth of the RAW kernels at two CTAs per SM: W raw stages are
-// 2 KB larger than swizzled ones, so three fit beside the aligned stages;
-// with only A raw the W stream keeps the plain kernel's four.
-constexpr int raw_pair_stages(int raw) { return raw == kRawA ? kPairStages : 3; }
+// Load-ring depth of the RAW kernels at two CTAs per SM: with one raw
+// operand the plain kernel's four stages fit (a raw W tile is aligned into
+// tensor memory, so it takes no aligned shared-memory stage); with both, a
+// stage holds both raw areas and three fit beside the two aligned A stages
+// and the split-K receive buffer.
+constexpr int raw_pair_stages(int raw) { return raw == (kRawW | kRawA) ? 3 : kPairStages; }
 
 template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
 cudaError_t set_attr() {
