@@ -130,9 +130,18 @@ __host__ __device__ constexpr uint32_t raw_area_bytes(int rows) {
   }
   return most;
 }
-// Warps 2..5 turn raw stages into swizzled ones (idle during the main loop
+// Warps 2..5 turn raw stages into aligned ones (idle during the main loop
 // otherwise): one per SM sub-partition, which is what bounds the shift.
+// When both operands are raw and the token tile is small (at most 32
+// tokens), warps 2..5 align W (into tensor memory) while warps 6 and 7
+// align A (into shared memory), so the two shifts of a stage run side by
+// side (32 x 4096 x 4090: 14.3 -> 14.0 us); a larger A tile is aligned by
+// warps 2..5 before W (two warps made M = 128 slower: 24.4 -> 29.7 us).
 constexpr int kShiftWarps = 4;
+__host__ __device__ constexpr bool split_shift(int raw, int bt) { return raw == (kRawW | kRawA) && bt <= 32; }
+__host__ __device__ constexpr int shift_warps(int raw, int bt) {
+  return split_shift(raw, bt) ? kShiftWarps + 2 : raw != 0 ? kShiftWarps : 0;
+}
 
 // BT: token tile (MMA N).  TN: W rows per CTA, one M = 128 MMA (and one TMEM
 // accumulator of BT columns) per 128 rows.  A 256-row tile moves W in 32 KB
@@ -293,24 +302,26 @@ __device__ __forceinline__ void store_shifted(const uint4 (&lo)[N], const uint4 
   for (int j = 0; j < N; ++j) *reinterpret_cast<uint4*>(out[j]) = shift_by<S>(lo[j], hi[j]);
 }
 
-// Rows [0, ROWS) of one raw load stage -> the swizzled K-major tile at dst.
-// Raw rows are taken in class order in warp steps of four rows (lane l:
-// row l / 8 of the four, chunk g = l % 8); shift warp w takes the
-// contiguous block of steps [w * ROWS / 16, (w + 1) * ROWS / 16), in
-// batches of up to four steps.  A batch of 16 rows inside one class (every
+// Rows [0, ROWS) of one raw load stage -> the swizzled K-major tile at dst,
+// by the NW shift warps W0, W0 + 1, ...  Raw rows are taken in class order
+// in warp steps of four rows (lane l: row l / 8 of the four, chunk
+// g = l % 8); shift warp w takes the contiguous block of steps
+// [w * ROWS / (4 NW), (w + 1) * ROWS / (4 NW)), in batches of up to four
+// steps.  A batch of 16 rows inside one class (every
 // W batch) has a warp-uniform shift, applied by a compile-time shift chosen
 // once per batch; batches that span classes (A tiles of 16 or 32 tokens in
 // 4 or 8 classes) shift per lane.  Each lane loads its two raw granules
 // itself.  `release` runs once every raw granule of this operand is in
 // registers, before the last batch is shifted and stored, so the load stage
 // is freed early.
-template <int ROWS, typename Release>
+template <int ROWS, int NW = kShiftWarps, int W0 = 2, int MAXB = 4, typename Release>
 __device__ __forceinline__ void shift_rows(const uint8_t* raw, uint8_t* dst, int classes, unsigned shifts,
                                            Release release) {
-  static_assert(ROWS % 16 == 0, "tile rows come in multiples of 16");
-  constexpr int kPerWarp = ROWS / 16;                  // warp steps per shift warp
-  constexpr int kBatch = kPerWarp < 4 ? kPerWarp : 4;  // steps whose loads are issued together
-  const int wq = (static_cast<int>(threadIdx.x) >> 5) - 2;  // shift warp 0..3
+  static_assert(ROWS % (4 * NW) == 0, "tile rows come in multiples of four per shift warp");
+  constexpr int kPerWarp = ROWS / (4 * NW);                  // warp steps per shift warp
+  constexpr int kBatch = kPerWarp < MAXB ? kPerWarp : MAXB;  // steps whose loads are issued together
+  static_assert(kPerWarp % kBatch == 0, "batches stay inside one shift warp's block of steps");
+  const int wq = (static_cast<int>(threadIdx.x) >> 5) - W0;  // shift warp 0..NW-1
   const int lane = threadIdx.x & 31;
   const int g = lane & 7;
   const int log_c = classes == 1 ? 0 : classes == 2 ? 1 : classes == 4 ? 2 : 3;
@@ -456,30 +467,45 @@ __device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, ui
     if constexpr (Cfg::kRawW_) ptx::tc_fence_after_sync();
     const uint8_t* load = smem + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
     uint8_t* aligned = smem + Cfg::kShiftBase + static_cast<uint32_t>(sst) * Cfg::kShiftBytes;
-    // The load stage is released (one arrival per warp) once the last raw
-    // operand's granules are in registers; A (smaller) goes first.
+    // The load stage is released (one arrival per shift warp) once that
+    // warp's raw granules are in registers.
     auto release = [&]() {
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(empty_bar(stage));
     };
     auto keep = []() {};
-    if constexpr (Cfg::kRawA_) {
+    constexpr bool kSplit = split_shift(RAW, BT);
+    // With the split, warps 6..7 align A and warps 2..5 align W; otherwise
+    // warps 2..5 align A (if raw), then W (if raw).
+    const bool a_warp = kSplit && (threadIdx.x >> 5) >= 2 + kShiftWarps;
+    if constexpr (kSplit) {
+      if (a_warp) {
+        // Batches of two steps (8 rows) keep a batch inside one row class
+        // for A tiles of 32 tokens in 4 classes.
+        shift_rows<BT, 2, 2 + kShiftWarps, 2>(load + Cfg::kLoadWBytes, aligned, args.a_classes, args.a_shifts,
+                                              release);
+        ptx::fence_proxy_async_smem();
+      }
+    } else if constexpr (Cfg::kRawA_) {
       if constexpr (Cfg::kRawW_) {
         shift_rows<BT>(load + Cfg::kLoadWBytes, aligned, args.a_classes, args.a_shifts, keep);
       } else {
         shift_rows<BT>(load + Cfg::kLoadWBytes, aligned, args.a_classes, args.a_shifts, release);
       }
+      ptx::fence_proxy_async_smem();
     }
     if constexpr (Cfg::kRawW_) {
       static_assert(TN == 128, "raw W tiles are one M = 128 MMA");
-      shift_w_tmem(load, tmem_d + Cfg::kWTmemCol + static_cast<uint32_t>(sst) * Cfg::kWTmemStageCols,
-                   args.w_classes, args.w_shifts, release);
-      ptx::tmem_st_wait();
-      ptx::tc_fence_before_sync();
+      if (!a_warp) {
+        shift_w_tmem(load, tmem_d + Cfg::kWTmemCol + static_cast<uint32_t>(sst) * Cfg::kWTmemStageCols,
+                     args.w_classes, args.w_shifts, release);
+        ptx::tmem_st_wait();
+        ptx::tc_fence_before_sync();
+      }
     }
-    // Every writer orders its stores before the tensor core's reads, then
-    // one arrival per warp (128 arrivals on one barrier serialise).
-    if constexpr (Cfg::kRawA_) ptx::fence_proxy_async_smem();
+    // Every writer orders its stores before the tensor core's reads (proxy
+    // fence or TMEM store wait above), then one arrival per warp (128
+    // arrivals on one barrier serialise).
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(sfull_bar(sst));
   }
@@ -591,10 +617,10 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
       ptx::mbar_init(full_bar(i), 1);
       // A load stage is free once the MMA has read it (tcgen05.commit) and,
       // in RAW kernels, once every shift warp has read its raw rows.
-      ptx::mbar_init(empty_bar(i), (RAW != 0 ? kShiftWarps : 0) + (kMmaReadsLoad ? 1 : 0));
+      ptx::mbar_init(empty_bar(i), shift_warps(RAW, BT) + (kMmaReadsLoad ? 1 : 0));
     }
     for (int i = 0; i < kShift; ++i) {
-      ptx::mbar_init(sfull_bar(i), kShiftWarps);
+      ptx::mbar_init(sfull_bar(i), shift_warps(RAW, BT));
       ptx::mbar_init(sempty_bar(i), 1);
     }
     ptx::mbar_init(done_bar, 1);
@@ -670,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
   // armed only after the main loop.
   const bool recv_dedicated = split > 1 && !args.recv_overlaps;
   // The shift warps (RAW) wait after their loop instead.
-  const bool shifter = RAW != 0 && warp >= 2 && warp < 2 + kShiftWarps;
+  const bool shifter = RAW != 0 && warp >= 2 && warp < 2 + shift_warps(RAW, BT);
   if (recv_dedicated) {
     ptx::cluster_arrive_relaxed();
     if (warp >= 2 && !shifter) ptx::cluster_wait();
