@@ -231,6 +231,7 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   c->tile_t = 0;
   c->tile_n = 128;
   c->stages = 0;
+  c->kps = 1;
   c->w_mn = 0;
   c->raw = 0;
   if (p.m == 0 || p.n == 0) {
@@ -295,6 +296,15 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   // Split-K tiles hold at most 128 tokens (the merge buffers must fit in the
   // drained pipeline memory).
   if (c->split > 1 && c->tile_t > 128) c->tile_t = 128;
+  // Split-K tiles of 128 W rows move two K blocks per TMA operation (32 KB
+  // of W) when K is whole blocks and every split gets an even number of
+  // them: the two-CTAs-per-SM split, and 64- or 128-token tiles.
+  const bool pair = c->stages == kPairStages;
+  if (c->split > 1 && c->tile_n == 128 && !L.w_mnmajor && !staged && kPairKps == 2 && p.k % 64 == 0 &&
+      k_blocks % c->split == 0 && (k_blocks / c->split) % 2 == 0 && kps2_stages(c->tile_t, pair) > 0) {
+    c->kps = 2;
+    c->stages = kps2_stages(c->tile_t, pair);
+  }
   // Prefill-sized problems (256-token tiles, no split) with at least one
   // wave of 256 x 256 output tiles: two M = 128 MMAs per K step share the
   // token tile, doubling the FLOPs per staged byte.
@@ -388,7 +398,7 @@ int launch_gather(GatherCall* call, unsigned int* counter, cudaStream_t s, int* 
   call->g.counter = counter;
   const Choice& c = call->c;
   const cudaError_t e =
-      launch_tc(call->p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, &call->g, call->dev->error_word, s);
+      launch_tc(call->p, c.split, c.tile_t, c.tile_n, c.stages, c.kps, c.w_mn, &call->g, call->dev->error_word, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return GLQ_ERR_CUDA;
@@ -516,7 +526,7 @@ int glq_linear_ex(int dtype, const void* A, int64_t a_row_stride, int64_t a_col_
     case glq::kKernelGemv: e = glq::launch_gemv(p, c.split, dev->error_word, s); break;
     case glq::kKernelGemvRing: e = glq::launch_gemv_ring(p, dev->error_word, s, dev->sm_count); break;
     case glq::kKernelTc:
-      e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.w_mn, nullptr, dev->error_word, s);
+      e = glq::launch_tc(p, c.split, c.tile_t, c.tile_n, c.stages, c.kps, c.w_mn, nullptr, dev->error_word, s);
       break;
     case glq::kKernelGeneric: e = glq::launch_generic(p, s); break;
     case glq::kKernelSmall: e = glq::launch_small(p, s); break;

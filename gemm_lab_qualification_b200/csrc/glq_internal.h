@@ -130,7 +130,8 @@ struct Choice {
   int kernel;   // Kernel below
   int tile_t;   // token tile (MMA N) of the tcgen05 kernel
   int tile_n;   // W rows per CTA of the tcgen05 kernel (128 or 256)
-  int stages;   // TMA ring depth of the tcgen05 kernel (5: two CTAs per SM)
+  int stages;   // TMA ring depth of the tcgen05 kernel (kPairStages: two CTAs per SM)
+  int kps;      // K blocks per TMA stage of the tcgen05 kernel (1, or 2 with 3-D boxes)
   int w_mn;     // 1: W = B^T is N-contiguous (B = [K, N]); MN-major W tiles
   int raw;      // kRawW | kRawA: operands staged raw and aligned by the tcgen05 kernel (path tc_ldg)
 };
@@ -167,6 +168,17 @@ constexpr int kMaxAutoSplit = 4;
 // co-resident at that size).
 constexpr int kPairSplit = 8;
 constexpr int kPairStages = 4;
+// The same split with two K blocks per stage: one 32 KB W box (and one A
+// box) per TMA operation, two stages (the same bytes in flight).
+constexpr int kPairStagesKps2 = 2;
+constexpr int kPairKps = 2;  // K blocks per stage the planner picks for that split when K allows
+// Ring depth of the two-K-blocks-per-stage kernels (half the one-block
+// depth, the same bytes in flight): the two-CTAs-per-SM split, and the
+// one-CTA-per-SM split-K tiles of 64 and 128 tokens; 0 where there is none.
+inline int kps2_stages(int tile_t, bool pair) {
+  if (pair) return tile_t <= 32 ? kPairStagesKps2 : 0;
+  return tile_t == 64 ? 4 : tile_t == 128 ? 3 : 0;
+}
 
 // Operands the tcgen05 kernel can stage raw and align itself are copied
 // instead when the caller gives a repack workspace and the problem has more
@@ -224,7 +236,9 @@ cudaError_t launch_repack(const void* src, int64_t rows, int64_t cols, int64_t r
 // Returns cudaErrorNotSupported-style codes through `status` for TMA encode
 // problems (GLQ_ERR_CUDA).
 // gather: null for a plain call (the output is p.y only).
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
+// kps: K blocks per load stage (2: 3-D TMA boxes of two K blocks, the
+// two-CTAs-per-SM split with stages == kPairStagesKps2).
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int kps, int w_mn,
                       const Gather* gather, unsigned int* err, cudaStream_t s);
 
 // Per-device one-time set-up of the tcgen05 kernels (shared memory opt-in).

@@ -93,6 +93,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int3
       : "memory");
 }
 
+// 3-D tiled bulk tensor load (one TMA operation for the whole box), as
+// tma_load_2d; x is the innermost coordinate.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int32_t x, int32_t y, int32_t z,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 // ---- cross-GPU completion protocol (fused gather): system-scope release /
 // acquire on 64-bit signal slots, and a GPU-scope acq_rel arrival counter.
 // Orders this thread's earlier memory operations (peer stores included)

@@ -150,26 +150,33 @@ __host__ __device__ constexpr int shift_warps(int raw, int bt) {
 // tile plus the split-K receive buffer keep a CTA under 113 KB of shared
 // memory, so two CTAs share an SM.
 //
+// KPS: K blocks per load stage.  With KPS = 2 (K-major, 128-row tiles, no
+// raw operand) one 3-D TMA box fetches a 32 KB W stage (two 16 KB K-major
+// tiles back to back) and another the two A tiles, so the W stream moves in
+// 32 KB operations without doubling the tile (and the split-K merge).
+//
 // Shared memory: STAGES load stages (what TMA writes: for each operand its
-// 128-byte-swizzled tile, or for a RAW operand its raw row boxes of 144
+// 128-byte-swizzled tile(s), or for a RAW operand its raw row boxes of 144
 // bytes per row), then, in RAW kernels, two aligned stages holding the
 // swizzled tiles of the RAW operands.
-template <int BT, int TN, int STAGES, int RAW = 0>
+template <int BT, int TN, int STAGES, int RAW = 0, int KPS = 1>
 struct TcConfig {
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128 is 16..256 step 16");
   static_assert(TN == 128 || TN == 256, "tile rows are one or two M=128 MMAs");
   static_assert(RAW == 0 || TN == 128, "raw-staged kernels use 128-row W tiles");
+  static_assert(KPS == 1 || (KPS == 2 && RAW == 0 && TN == 128), "two K blocks per stage: plain 128-row tiles");
   static constexpr bool kRawW_ = (RAW & kRawW) != 0;
   static constexpr bool kRawA_ = (RAW & kRawA) != 0;
   static constexpr int kAcc = TN / 128;
-  static constexpr uint32_t kWTileBytes = TN * kTileK * 2;
-  static constexpr uint32_t kATileBytes = BT * kTileK * 2;
+  static constexpr int kKps = KPS;
+  static constexpr uint32_t kWTileBytes = TN * kTileK * 2;  // one K block
+  static constexpr uint32_t kATileBytes = BT * kTileK * 2;  // one K block
   // Load stage: the W part first, then A (1024-byte aligned when swizzled).
-  static constexpr uint32_t kLoadWBytes = kRawW_ ? raw_area_bytes(TN) : kWTileBytes;
-  static constexpr uint32_t kLoadABytes = kRawA_ ? raw_area_bytes(BT) : kATileBytes;
+  static constexpr uint32_t kLoadWBytes = kRawW_ ? raw_area_bytes(TN) : KPS * kWTileBytes;
+  static constexpr uint32_t kLoadABytes = kRawA_ ? raw_area_bytes(BT) : KPS * kATileBytes;
   // Bytes TMA lands per stage (every box counts in full, zero fill included).
   static constexpr uint32_t kLoadTx =
-      (kRawW_ ? TN * kRawRowBytes : kWTileBytes) + (kRawA_ ? BT * kRawRowBytes : kATileBytes);
+      (kRawW_ ? TN * kRawRowBytes : KPS * kWTileBytes) + (kRawA_ ? BT * kRawRowBytes : KPS * kATileBytes);
   // Load stages holding a swizzled tile start 1024-byte aligned; raw-only
   // stages need the TMA's 128 bytes.
   static constexpr uint32_t kStageAlign = (kRawW_ && kRawA_) ? 128u : 1024u;
@@ -514,11 +521,12 @@ __device__ __forceinline__ void shift_loop(const TcArgs& args, uint8_t* smem, ui
 // RAW: operands TMA cannot address are staged raw and aligned by warps 2..5
 // (K-major W, 128-row tiles, no gather); two CTAs per SM must still fit, so
 // these instantiations are capped at 128 registers.
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0, int KPS = 1>
 __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
     tc_linear_kernel(const __grid_constant__ TmaSet<RAW> maps, const TcArgs args) {
   static_assert(RAW == 0 || (!WMN && !GATHER && TN == 128), "raw-staged operands: K-major 128-row tiles only");
-  using Cfg = TcConfig<BT, TN, STAGES, RAW>;
+  static_assert(KPS == 1 || !WMN, "two K blocks per stage: K-major W");
+  using Cfg = TcConfig<BT, TN, STAGES, RAW, KPS>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kShift = Cfg::kShift;
   // The MMA reads a load stage directly unless both operands are raw.
@@ -546,6 +554,9 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
   const int kb_begin = static_cast<int>((static_cast<long long>(s) * args.num_kb) / split);
   const int kb_end = static_cast<int>((static_cast<long long>(s + 1) * args.num_kb) / split);
   const int nkb = kb_end - kb_begin;
+  // Load stages of this CTA (KPS K blocks each; the planner gives every CTA
+  // a multiple of KPS blocks).
+  const int nst = (nkb + KPS - 1) / KPS;
 
   auto full_bar = [&](int i) { return ptx::smem_addr(&bars[i]); };
   auto empty_bar = [&](int i) { return ptx::smem_addr(&bars[kStages + i]); };
@@ -574,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
   auto issue_w = [&](int i) {
     const int stage = i % kStages;
     const uint32_t w_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes;
-    const int k0 = (kb_begin + i) * kTileK;
+    const int k0 = (kb_begin + i * KPS) * kTileK;
     ptx::mbar_arrive_expect_tx(full_bar(stage), Cfg::kLoadTx);
     if constexpr (Cfg::kRawW_) {
       // One box of TN / C rows x 72 elements per row class, unswizzled.
@@ -590,6 +601,9 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
         ptx::tma_load_2d(w_dst + static_cast<uint32_t>(j) * kMnBoxBytes, &maps.w[0], tile_n * TN + 64 * j, k0,
                          full_bar(stage), pol_w);
       }
+    } else if constexpr (KPS == 2) {
+      // One 64 x TN x 2 box: two K-major tiles of consecutive K blocks.
+      ptx::tma_load_3d(w_dst, &maps.w[0], 0, tile_n * TN, kb_begin + i * KPS, full_bar(stage), pol_w);
     } else {
       ptx::tma_load_2d(w_dst, &maps.w[0], k0, tile_n * TN, full_bar(stage), pol_w);
     }
@@ -597,13 +611,15 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
   auto issue_a = [&](int i) {
     const int stage = i % kStages;
     const uint32_t a_dst = sbase + static_cast<uint32_t>(stage) * Cfg::kStageBytes + Cfg::kLoadWBytes;
-    const int k0 = (kb_begin + i) * kTileK;
+    const int k0 = (kb_begin + i * KPS) * kTileK;
     if constexpr (Cfg::kRawA_) {
       const int rows = BT / args.a_classes;
       for (int c = 0; c < args.a_classes; ++c) {
         ptx::tma_load_2d(a_dst + raw_class_offset(c, rows), &maps.a[c], k0,
                          tile_t * rows, full_bar(stage), pol_a);
       }
+    } else if constexpr (KPS == 2) {
+      ptx::tma_load_3d(a_dst, &maps.a[0], 0, tile_t * BT, kb_begin + i * KPS, full_bar(stage), pol_a);
     } else {
       ptx::tma_load_2d(a_dst, &maps.a[0], k0, tile_t * BT, full_bar(stage), pol_a);
     }
@@ -642,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
     // the predecessor kernel may still be running: A (and W unless the
     // caller declared the weights static) is read only after the dependency
     // wait.
-    const int first = nkb < kStages ? nkb : kStages;
+    const int first = nst < kStages ? nst : kStages;
     const bool static_w = RAW == 0 && (args.flags & GLQ_FLAG_STATIC_WEIGHTS) != 0;
     if (static_w) {
       for (int i = 0; i < first; ++i) issue_w(i);
@@ -704,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = issued; i < nkb; ++i) {
+      for (int i = issued; i < nst; ++i) {
         const int stage = i % kStages;
         const uint32_t round = static_cast<uint32_t>(i / kStages);
         if (!ptx::mbar_wait_bounded(empty_bar(stage), (round - 1u) & 1u, abort_flag, kWaitBudgetNs)) {
@@ -724,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
       // Descriptor start-address step (16-byte units) per K = 16 MMA: 32 B
       // along a K-major swizzled row, or 16 K rows of 128 B when MN-major.
       constexpr uint32_t kWStep = WMN ? 128u : 2u;
-      for (int i = 0; i < nkb; ++i) {
+      for (int i = 0; i < nst; ++i) {
         const int stage = i % kStages;
         const uint32_t round = static_cast<uint32_t>(i / kStages);
         const int sst = kShift > 0 ? i % kShift : 0;
@@ -753,13 +769,21 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
         } else {
           const uint64_t w_desc = WMN ? ptx::umma_desc_mn_sw128(load) : ptx::umma_desc_k_sw128(load);
 #pragma unroll
-          for (int kk = 0; kk < kTileK / 16; ++kk) {
-            // Each MMA consumes K = 16.  The 128-row halves of a 256-row W
-            // tile are 16 KB (1024 units) apart in both layouts.
+          for (int j = 0; j < KPS; ++j) {
+            // K block j of the stage: its W and A tiles follow those of
+            // block j - 1 (descriptor addresses in 16-byte units).
+            if (j > 0 && i * KPS + j >= nkb) break;
 #pragma unroll
-            for (int h = 0; h < Cfg::kAcc; ++h) {
-              ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT), w_desc + 1024u * h + kWStep * kk,
-                              a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kTileK / 16; ++kk) {
+              // Each MMA consumes K = 16.  The 128-row halves of a 256-row W
+              // tile are 16 KB (1024 units) apart in both layouts.
+#pragma unroll
+              for (int h = 0; h < Cfg::kAcc; ++h) {
+                ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT),
+                                w_desc + (Cfg::kWTileBytes >> 4) * j + 1024u * h + kWStep * kk,
+                                a_desc + (Cfg::kATileBytes >> 4) * j + 2u * kk, idesc,
+                                (i > 0 || j > 0 || kk > 0) ? 1u : 0u);
+              }
             }
           }
         }
@@ -1093,6 +1117,26 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   return r == CUDA_SUCCESS;
 }
 
+// 3-D map of a row-major matrix rows x k (K contiguous, k a multiple of 64)
+// seen as [k / 64 blocks][rows][64]: dims {64, rows, k / 64}, strides
+// {row pitch, 128 bytes}; a box of 64 x box_rows x 2 lands as two
+// consecutive 128-byte-swizzled K-major tiles (two K blocks), which is what
+// two 2-D boxes of 64 x box_rows at consecutive K blocks would give.
+bool encode_kblocks_3d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int64_t k, int64_t rows,
+                       int64_t row_pitch_bytes, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encoder();
+  if (encode == nullptr || k % kTileK != 0) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kTileK), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(k / kTileK)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_pitch_bytes), static_cast<cuuint64_t>(kTileK * 2)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTileK), box_rows, 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, type, 3, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // One map per row class of a raw operand (rows x k, K contiguous, row pitch
 // `pitch` elements, 2-byte aligned base): class c's rows r = c, c + C, ...
 // as a 2-D tensor of (k + s_c) x rows_c elements, origin at the 16-byte
@@ -1139,9 +1183,9 @@ bool encode_raw(CUtensorMap* maps, CUtensorMapDataType type, const void* base, i
 // and the split-K receive buffer.
 constexpr int raw_pair_stages(int raw) { return raw == (kRawW | kRawA) ? 3 : kPairStages; }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0, int KPS = 1>
 cudaError_t set_attr() {
-  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, RAW>,
+  return cudaFuncSetAttribute(tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, RAW, KPS>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
 }
 
@@ -1180,12 +1224,21 @@ cudaError_t set_attrs_all() {
   if ((e = set_attrs<T, 64, 128, 8>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 128, 128, 6>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 256, 128, 4>()) != cudaSuccess) return e;
+  // Two K blocks per stage (3-D boxes) for the two-CTAs-per-SM split.
+  if ((e = set_attr<T, 16, 128, kPairStagesKps2, false, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 32, 128, kPairStagesKps2, false, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 16, 128, kPairStagesKps2, false, true, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 32, 128, kPairStagesKps2, false, true, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 64, 128, 4, false, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 64, 128, 4, false, true, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 128, 128, 3, false, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 128, 128, 3, false, true, 0, 2>()) != cudaSuccess) return e;
   if ((e = set_attrs_raw<T, kRawW>()) != cudaSuccess) return e;
   if ((e = set_attrs_raw<T, kRawA>()) != cudaSuccess) return e;
   return set_attrs_raw<T, kRawW | kRawA>();
 }
 
-template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0>
+template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW = 0, int KPS = 1>
 cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned int* err, cudaStream_t stream) {
   constexpr int64_t esz = 2;
   TmaSet<RAW> maps;
@@ -1198,19 +1251,21 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
     // B = [K, N]: rows k (pitch b_ks), N contiguous; boxes 64(n) x 64(k).
     ok = encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
   } else {
-    // W = B^T: rows n (pitch b_ns), K contiguous; boxes 64(k) x TN.
+    // W = B^T: rows n (pitch b_ns), K contiguous; boxes 64(k) x TN (x 2 K blocks).
     const int64_t w_pitch = p.n > 1 ? p.b_ns * esz : ((p.k * esz + 15) / 16) * 16;
-    ok = encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, kTileK, TN);
+    ok = KPS == 2 ? encode_kblocks_3d(&maps.w[0], Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, TN)
+                  : encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.k, p.n, w_pitch, kTileK, TN);
   }
   if constexpr ((RAW & kRawA) != 0) {
     ok = ok && encode_raw(maps.a, Elem<T>::kTmaType, p.a, p.m, p.k, p.a_rs, BT, &a_rc);
   } else {
-    // A: rows m (pitch a_rs), K contiguous; boxes 64(k) x BT.
+    // A: rows m (pitch a_rs), K contiguous; boxes 64(k) x BT (x 2 K blocks).
     const int64_t a_pitch = p.m > 1 ? p.a_rs * esz : ((p.k * esz + 15) / 16) * 16;
-    ok = ok && encode_2d(&maps.a[0], Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, kTileK, BT);
+    ok = ok && (KPS == 2 ? encode_kblocks_3d(&maps.a[0], Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, BT)
+                         : encode_2d(&maps.a[0], Elem<T>::kTmaType, p.a, p.k, p.m, a_pitch, kTileK, BT));
   }
   if (!ok) return cudaErrorInvalidValue;
-  using Cfg = TcConfig<BT, TN, STAGES, RAW>;
+  using Cfg = TcConfig<BT, TN, STAGES, RAW, KPS>;
   // The raw boxes of the operands' row classes must fit their load-stage areas.
   if constexpr ((RAW & kRawW) != 0) {
     if (raw_class_offset(w_rc.classes, TN / w_rc.classes) > Cfg::kLoadWBytes) return cudaErrorInvalidValue;
@@ -1266,7 +1321,8 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
     stage_bytes = TN * groups * 16u;
   }
   // The two-CTAs-per-SM configuration keeps under half an SM.
-  constexpr bool kPair = TN == 128 && BT <= 32 && STAGES == (RAW != 0 ? raw_pair_stages(RAW) : kPairStages);
+  constexpr bool kPair = TN == 128 && BT <= 32 &&
+                         STAGES == (KPS == 2 ? kPairStagesKps2 : RAW != 0 ? raw_pair_stages(RAW) : kPairStages);
   const uint32_t budget = kPair ? kPairSmemBudget : kSmemLimit;
   const bool dedicated = 1024 + Cfg::kPipeBytes + recv_bytes + Cfg::kBarrierBytes <= budget;
   args.recv_offset = dedicated ? Cfg::kPipeBytes : 0;
@@ -1309,7 +1365,7 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (p.flags & GLQ_FLAG_NO_PDL) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, RAW>, maps, args);
+  return cudaLaunchKernelEx(&cfg, tc_linear_kernel<T, BT, TN, STAGES, WMN, GATHER, RAW, KPS>, maps, args);
 }
 
 // Operands TMA cannot address as they are: the RAW kernels (128-row tiles).
@@ -1347,8 +1403,22 @@ cudaError_t launch_raw_any(const Problem& p, int split, int tile_t, int tile_n, 
 }
 
 template <typename T, bool WMN, bool GATHER>
-cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, const Gather* g,
+cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, int kps, const Gather* g,
                       unsigned int* err, cudaStream_t s) {
+  if (kps == 2) {
+    if constexpr (WMN) {
+      return cudaErrorInvalidValue;
+    } else {
+      if (tile_n != 128 || stages != kps2_stages(tile_t, stages == kPairStagesKps2)) return cudaErrorInvalidValue;
+      switch (tile_t) {
+        case 16: return launch_typed<T, 16, 128, kPairStagesKps2, false, GATHER, 0, 2>(p, split, g, err, s);
+        case 32: return launch_typed<T, 32, 128, kPairStagesKps2, false, GATHER, 0, 2>(p, split, g, err, s);
+        case 64: return launch_typed<T, 64, 128, 4, false, GATHER, 0, 2>(p, split, g, err, s);
+        case 128: return launch_typed<T, 128, 128, 3, false, GATHER, 0, 2>(p, split, g, err, s);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+  }
   if (tile_n == 256) {
     switch (tile_t) {
       case 16: return launch_typed<T, 16, 256, 4, WMN, GATHER>(p, split, g, err, s);
@@ -1382,7 +1452,7 @@ cudaError_t tc_prepare_device() {
   return set_attrs_all<__nv_bfloat16>();
 }
 
-cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int w_mn,
+cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int stages, int kps, int w_mn,
                       const Gather* g, unsigned int* err, cudaStream_t s) {
   if (p.raw != 0) {
     if (g != nullptr || w_mn) return cudaErrorInvalidValue;
@@ -1391,18 +1461,18 @@ cudaError_t launch_tc(const Problem& p, int split, int tile_t, int tile_n, int s
   }
   if (g != nullptr) {
     if (p.dtype == GLQ_DTYPE_BF16) {
-      return w_mn ? launch_bt<__nv_bfloat16, true, true>(p, split, tile_t, tile_n, stages, g, err, s)
-                  : launch_bt<__nv_bfloat16, false, true>(p, split, tile_t, tile_n, stages, g, err, s);
+      return w_mn ? launch_bt<__nv_bfloat16, true, true>(p, split, tile_t, tile_n, stages, kps, g, err, s)
+                  : launch_bt<__nv_bfloat16, false, true>(p, split, tile_t, tile_n, stages, kps, g, err, s);
     }
-    return w_mn ? launch_bt<__half, true, true>(p, split, tile_t, tile_n, stages, g, err, s)
-                : launch_bt<__half, false, true>(p, split, tile_t, tile_n, stages, g, err, s);
+    return w_mn ? launch_bt<__half, true, true>(p, split, tile_t, tile_n, stages, kps, g, err, s)
+                : launch_bt<__half, false, true>(p, split, tile_t, tile_n, stages, kps, g, err, s);
   }
   if (p.dtype == GLQ_DTYPE_BF16) {
-    return w_mn ? launch_bt<__nv_bfloat16, true, false>(p, split, tile_t, tile_n, stages, g, err, s)
-                : launch_bt<__nv_bfloat16, false, false>(p, split, tile_t, tile_n, stages, g, err, s);
+    return w_mn ? launch_bt<__nv_bfloat16, true, false>(p, split, tile_t, tile_n, stages, kps, g, err, s)
+                : launch_bt<__nv_bfloat16, false, false>(p, split, tile_t, tile_n, stages, kps, g, err, s);
   }
-  return w_mn ? launch_bt<__half, true, false>(p, split, tile_t, tile_n, stages, g, err, s)
-              : launch_bt<__half, false, false>(p, split, tile_t, tile_n, stages, g, err, s);
+  return w_mn ? launch_bt<__half, true, false>(p, split, tile_t, tile_n, stages, kps, g, err, s)
+              : launch_bt<__half, false, false>(p, split, tile_t, tile_n, stages, kps, g, err, s);
 }
 
 }  // namespace glq
