@@ -297,10 +297,11 @@ int plan_problem(const Problem& p, int split_k, int sm_count, Choice* c) {
   // drained pipeline memory).
   if (c->split > 1 && c->tile_t > 128) c->tile_t = 128;
   // Split-K tiles of 128 W rows move two K blocks per TMA operation (32 KB
-  // of W) when K is whole blocks and every split gets an even number of
-  // them: the two-CTAs-per-SM split, and 64- or 128-token tiles.
+  // of W) when K is whole blocks (and, for the lab's B = [K, N], N whole
+  // blocks of 64 columns) and every split gets an even number of them: the
+  // two-CTAs-per-SM split, and 64- or 128-token tiles.
   const bool pair = c->stages == kPairStages;
-  if (c->split > 1 && c->tile_n == 128 && !L.w_mnmajor && !staged && kPairKps == 2 && p.k % 64 == 0 &&
+  if (c->split > 1 && c->tile_n == 128 && (!L.w_mnmajor || p.n % 64 == 0) && !staged && kPairKps == 2 && p.k % 64 == 0 &&
       k_blocks % c->split == 0 && (k_blocks / c->split) % 2 == 0 && kps2_stages(c->tile_t, pair) > 0) {
     c->kps = 2;
     c->stages = kps2_stages(c->tile_t, pair);

@@ -311,10 +311,12 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_byte_addr) {
 // box is 128 contiguous bytes, 8-row K groups are 1024 B apart (stride byte
 // offset) and the second 64-element MN half is the next box, 8192 B later
 // (leading byte offset).  Same version / layout-type fields as above.
-__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_byte_addr) {
+// lbo_bytes: distance between the two 64-element MN halves (8 KB for one K
+// block of 64 rows per box, 16 KB when a box holds two K blocks).
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_byte_addr, uint32_t lbo_bytes = 8192u) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(8192u >> 4) << 16;
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>(1024u >> 4) << 32;
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;

@@ -230,6 +230,7 @@ struct TcArgs {
   int recv_overlaps;        // 1: the receive buffer reuses the drained pipeline stages
   uint32_t barrier_offset;  // mbarriers, bytes from the aligned base
   unsigned int flags;       // glq_flags
+  int w_3d;                 // MN-major W (WMN): one 3-D box per stage instead of TN / 64 2-D boxes
   // RAW kernels: rows of a raw operand are split into C classes (row
   // r in class r % C, C a power of two); class c's rows start s_c elements
   // into a 16-byte granule, 4 bits per class in *_shifts.
@@ -525,7 +526,6 @@ template <typename T, int BT, int TN, int STAGES, bool WMN, bool GATHER, int RAW
 __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
     tc_linear_kernel(const __grid_constant__ TmaSet<RAW> maps, const TcArgs args) {
   static_assert(RAW == 0 || (!WMN && !GATHER && TN == 128), "raw-staged operands: K-major 128-row tiles only");
-  static_assert(KPS == 1 || !WMN, "two K blocks per stage: K-major W");
   using Cfg = TcConfig<BT, TN, STAGES, RAW, KPS>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kShift = Cfg::kShift;
@@ -595,11 +595,17 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
                          tile_n * rows, full_bar(stage), pol_w);
       }
     } else if constexpr (WMN) {
-      // TN/64 boxes of 64 N-contiguous W rows x 64 K rows, 8 KB apart.
+      if (KPS == 2 || args.w_3d) {
+        // One box of 64 N-contiguous W rows x 64 * KPS K rows x TN / 64
+        // column blocks: the column blocks land 64 * KPS * 128 B apart.
+        ptx::tma_load_3d(w_dst, &maps.w[0], 0, k0, tile_n * (TN / 64), full_bar(stage), pol_w);
+      } else {
+        // TN/64 boxes of 64 N-contiguous W rows x 64 K rows, 8 KB apart.
 #pragma unroll
-      for (int j = 0; j < TN / 64; ++j) {
-        ptx::tma_load_2d(w_dst + static_cast<uint32_t>(j) * kMnBoxBytes, &maps.w[0], tile_n * TN + 64 * j, k0,
-                         full_bar(stage), pol_w);
+        for (int j = 0; j < TN / 64; ++j) {
+          ptx::tma_load_2d(w_dst + static_cast<uint32_t>(j) * kMnBoxBytes, &maps.w[0], tile_n * TN + 64 * j, k0,
+                           full_bar(stage), pol_w);
+        }
       }
     } else if constexpr (KPS == 2) {
       // One 64 x TN x 2 box: two K-major tiles of consecutive K blocks.
@@ -767,7 +773,11 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
             ptx::tc_mma_f16_ts(tmem_d, w_tmem + 8u * kk, a_desc + 2u * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
           }
         } else {
-          const uint64_t w_desc = WMN ? ptx::umma_desc_mn_sw128(load) : ptx::umma_desc_k_sw128(load);
+          // MN-major boxes of two K blocks put the 64-element column blocks
+          // 16 KB apart and the second K block 8 KB into each.
+          const uint64_t w_desc =
+              WMN ? ptx::umma_desc_mn_sw128(load, KPS * kMnBoxBytes) : ptx::umma_desc_k_sw128(load);
+          constexpr uint32_t kWBlockStep = WMN ? (kMnBoxBytes >> 4) : (Cfg::kWTileBytes >> 4);
 #pragma unroll
           for (int j = 0; j < KPS; ++j) {
             // K block j of the stage: its W and A tiles follow those of
@@ -780,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, RAW != 0 ? 2 : 1)
 #pragma unroll
               for (int h = 0; h < Cfg::kAcc; ++h) {
                 ptx::tc_mma_f16(tmem_d + static_cast<uint32_t>(h * BT),
-                                w_desc + (Cfg::kWTileBytes >> 4) * j + 1024u * h + kWStep * kk,
+                                w_desc + kWBlockStep * j + 1024u * KPS * h + kWStep * kk,
                                 a_desc + (Cfg::kATileBytes >> 4) * j + 2u * kk, idesc,
                                 (i > 0 || j > 0 || kk > 0) ? 1u : 0u);
               }
@@ -1137,6 +1147,25 @@ bool encode_kblocks_3d(CUtensorMap* map, CUtensorMapDataType type, const void* b
   return r == CUDA_SUCCESS;
 }
 
+// 3-D map of the lab's B = [K, N] (N contiguous, n a multiple of 64) seen
+// as [n / 64 column blocks][k][64]: dims {64, k, n / 64}, strides {row pitch,
+// 128 bytes}; a box of 64 x box_k x box_blocks lands box_blocks MN-major
+// 128-byte-swizzled tiles of 64 columns x box_k rows back to back, which is
+// what box_blocks 2-D boxes of 64 x box_k would write.
+bool encode_mn_3d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int64_t n, int64_t k,
+                  int64_t row_pitch_bytes, uint32_t box_k, uint32_t box_blocks) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encoder();
+  if (encode == nullptr || n % 64 != 0) return false;
+  const cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(n / 64)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_pitch_bytes), 128u};
+  const cuuint32_t box[3] = {64u, box_k, box_blocks};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, type, 3, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // One map per row class of a raw operand (rows x k, K contiguous, row pitch
 // `pitch` elements, 2-byte aligned base): class c's rows r = c, c + C, ...
 // as a 2-D tensor of (k + s_c) x rows_c elements, origin at the 16-byte
@@ -1189,6 +1218,19 @@ cudaError_t set_attr() {
                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
 }
 
+template <typename T, bool WMN>
+cudaError_t set_attrs_kps2() {
+  cudaError_t e;
+  if ((e = set_attr<T, 16, 128, kPairStagesKps2, WMN, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 32, 128, kPairStagesKps2, WMN, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 16, 128, kPairStagesKps2, WMN, true, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 32, 128, kPairStagesKps2, WMN, true, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 64, 128, 4, WMN, false, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 64, 128, 4, WMN, true, 0, 2>()) != cudaSuccess) return e;
+  if ((e = set_attr<T, 128, 128, 3, WMN, false, 0, 2>()) != cudaSuccess) return e;
+  return set_attr<T, 128, 128, 3, WMN, true, 0, 2>();
+}
+
 template <typename T, int RAW>
 cudaError_t set_attrs_raw() {
   cudaError_t e;
@@ -1224,15 +1266,9 @@ cudaError_t set_attrs_all() {
   if ((e = set_attrs<T, 64, 128, 8>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 128, 128, 6>()) != cudaSuccess) return e;
   if ((e = set_attrs<T, 256, 128, 4>()) != cudaSuccess) return e;
-  // Two K blocks per stage (3-D boxes) for the two-CTAs-per-SM split.
-  if ((e = set_attr<T, 16, 128, kPairStagesKps2, false, false, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 32, 128, kPairStagesKps2, false, false, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 16, 128, kPairStagesKps2, false, true, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 32, 128, kPairStagesKps2, false, true, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 64, 128, 4, false, false, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 64, 128, 4, false, true, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 128, 128, 3, false, false, 0, 2>()) != cudaSuccess) return e;
-  if ((e = set_attr<T, 128, 128, 3, false, true, 0, 2>()) != cudaSuccess) return e;
+  // Two K blocks per stage (3-D boxes) for the split-K tiles of 128 W rows.
+  if ((e = set_attrs_kps2<T, false>()) != cudaSuccess) return e;
+  if ((e = set_attrs_kps2<T, true>()) != cudaSuccess) return e;
   if ((e = set_attrs_raw<T, kRawW>()) != cudaSuccess) return e;
   if ((e = set_attrs_raw<T, kRawA>()) != cudaSuccess) return e;
   return set_attrs_raw<T, kRawW | kRawA>();
@@ -1244,12 +1280,17 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   TmaSet<RAW> maps;
   RawClasses w_rc, a_rc;
   bool ok = true;
+  bool w_3d = false;
   if constexpr ((RAW & kRawW) != 0) {
     // W rows TMA cannot address as they are: one unswizzled map per row class.
     ok = encode_raw(maps.w, Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ns, TN, &w_rc);
   } else if constexpr (WMN) {
-    // B = [K, N]: rows k (pitch b_ks), N contiguous; boxes 64(n) x 64(k).
-    ok = encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
+    // B = [K, N]: rows k (pitch b_ks), N contiguous; one 3-D box of
+    // 64(n) x 64 * KPS(k) x TN / 64 column blocks when N is whole blocks of 64,
+    // else TN / 64 boxes of 64(n) x 64(k).
+    w_3d = KPS == 2 || p.n % 64 == 0;
+    ok = w_3d ? encode_mn_3d(&maps.w[0], Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, kTileK * KPS, TN / 64)
+              : encode_2d(&maps.w[0], Elem<T>::kTmaType, p.b, p.n, p.k, p.b_ks * esz, 64, kTileK);
   } else {
     // W = B^T: rows n (pitch b_ns), K contiguous; boxes 64(k) x TN (x 2 K blocks).
     const int64_t w_pitch = p.n > 1 ? p.b_ns * esz : ((p.k * esz + 15) / 16) * 16;
@@ -1303,6 +1344,7 @@ cudaError_t launch_typed(const Problem& p, int split, const Gather* g, unsigned 
   args.partial = p.partial;
   args.err = err;
   args.flags = p.flags;
+  args.w_3d = w_3d ? 1 : 0;
   args.w_classes = w_rc.classes;
   args.w_shifts = w_rc.shifts;
   args.a_classes = a_rc.classes;
@@ -1406,17 +1448,13 @@ template <typename T, bool WMN, bool GATHER>
 cudaError_t launch_bt(const Problem& p, int split, int tile_t, int tile_n, int stages, int kps, const Gather* g,
                       unsigned int* err, cudaStream_t s) {
   if (kps == 2) {
-    if constexpr (WMN) {
-      return cudaErrorInvalidValue;
-    } else {
-      if (tile_n != 128 || stages != kps2_stages(tile_t, stages == kPairStagesKps2)) return cudaErrorInvalidValue;
-      switch (tile_t) {
-        case 16: return launch_typed<T, 16, 128, kPairStagesKps2, false, GATHER, 0, 2>(p, split, g, err, s);
-        case 32: return launch_typed<T, 32, 128, kPairStagesKps2, false, GATHER, 0, 2>(p, split, g, err, s);
-        case 64: return launch_typed<T, 64, 128, 4, false, GATHER, 0, 2>(p, split, g, err, s);
-        case 128: return launch_typed<T, 128, 128, 3, false, GATHER, 0, 2>(p, split, g, err, s);
-        default: return cudaErrorInvalidValue;
-      }
+    if (tile_n != 128 || stages != kps2_stages(tile_t, stages == kPairStagesKps2)) return cudaErrorInvalidValue;
+    switch (tile_t) {
+      case 16: return launch_typed<T, 16, 128, kPairStagesKps2, WMN, GATHER, 0, 2>(p, split, g, err, s);
+      case 32: return launch_typed<T, 32, 128, kPairStagesKps2, WMN, GATHER, 0, 2>(p, split, g, err, s);
+      case 64: return launch_typed<T, 64, 128, 4, WMN, GATHER, 0, 2>(p, split, g, err, s);
+      case 128: return launch_typed<T, 128, 128, 3, WMN, GATHER, 0, 2>(p, split, g, err, s);
+      default: return cudaErrorInvalidValue;
     }
   }
   if (tile_n == 256) {
